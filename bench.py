@@ -1,0 +1,383 @@
+"""Decode throughput of the B200 stage executor (Llama-3-8B architecture).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: Llama-3-8B geometry (32 layers, hidden 4096, 32 q / 8 KV heads,
+head_dim 128, intermediate 14336, vocab 128256, RoPE theta 5e5), bf16,
+synthetic random-init N(0, 0.02) weights, batch 32 as 4 micro-batches (request
+contexts) of 8, prompts of 1024 uniform-random ids, greedy decode.  A step is
+one decode token for all 32 rows.  N > 1 runs one pipeline stage per GPU
+(launched by torchrun), layers split evenly, hidden states between stages over
+NCCL, micro-batches in flight across stages.
+
+The JSON line reports decode tok/s (device-timed, inputs resident), the same
+metric end to end through the public API with host buffers (``e2e``), the
+roofline of the dominant kernel (the weight-streaming decode GEMMs) and of
+decode attention against the measured HBM copy bandwidth, and the CPU oracle
+timed on the host cores as a baseline.  ``--impl reference`` times only that
+CPU path (the reference's algorithm restated by the oracle; the reference
+itself is Python code that does not travel to the GPU host).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s (Llama-3-8B arch, 1/2/4/8 B200 stages); attn-decode HBM % of peak"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def llama3_8b():
+    from gpu_mesh_b200.config import LlamaConfig
+
+    return LlamaConfig(
+        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192,
+        rms_norm_eps=1e-5, rope_theta=500000.0,
+    )
+
+
+def peaks() -> tuple[float, float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int) -> None:
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {
+            "sm_mhz": sm[len(sm) // 2] if sm else None,
+            "sm_max_mhz": mx,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (the reference's algorithm) on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_baseline(cfg, *, micro: int, context: int, steps: int, weights_from=None) -> dict:
+    """Time the CPU oracle on a bounded sample of the decode workload.
+
+    Sample: one micro-batch of ``micro`` rows, every layer's KV cache pre-filled
+    to ``context`` positions with N(0, 1) bf16 values (the cost of a decode step
+    does not depend on how the prefix was produced), ``steps`` greedy decode
+    steps through all layers and the lm_head.
+    """
+    from oracle import stage_ref as R
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from gpu_mesh_b200.weights import synthetic_tensor, stage_keys
+
+    state = {}
+    for local, global_key, shape in stage_keys(cfg, 0, cfg.num_hidden_layers, True, True):
+        if weights_from is not None and local in weights_from:
+            state[local] = weights_from[local]
+        else:
+            dev = "cuda" if torch.cuda.is_available() else "cpu"
+            state[local] = synthetic_tensor(global_key, shape, seed=0, dtype=torch.bfloat16, device=dev).cpu()
+    st = R.OracleStage(cfg, 0, cfg.num_hidden_layers, True, True, state, torch.bfloat16)
+    g = torch.Generator().manual_seed(0)
+    kv = []
+    for _ in range(cfg.num_hidden_layers):
+        shape = (micro, cfg.num_key_value_heads, context, cfg.head_dim)
+        kv.append((torch.randn(shape, generator=g).to(torch.bfloat16),
+                   torch.randn(shape, generator=g).to(torch.bfloat16)))
+    st.caches["b"] = kv
+    ids = torch.randint(0, cfg.vocab_size, (micro, 1), generator=g)
+    with torch.no_grad():
+        st.forward(input_ids=ids, key="b")  # warm-up
+        st.trim(context, "b")
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            logits = st.forward(input_ids=ids, key="b")
+            ids = R.greedy(logits[:, -1]).unsqueeze(-1)
+        dt = time.perf_counter() - t0
+    return {
+        "value": micro * steps / dt,
+        "unit": "tok/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"oracle (CPU restatement of the reference stage), Llama-3-8B bf16, {micro} rows, "
+                   f"KV pre-filled to {context} positions, {steps} greedy decode steps, "
+                   f"{threads} threads"),
+        "seconds": dt,
+    }
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = llama3_8b()
+    base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=max(1, min(args.steps, 2)))
+    steps = args.steps
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": "tok/s",
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * args.micro / base["value"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {
+        "workload": "Llama-3-8B-architecture bf16 greedy decode, batch 32 as 4 micro-batches of 8, "
+                    f"{args.prompt}-token prompts",
+        "batch": args.micro * args.micro_batches,
+        "micro_batches": args.micro_batches,
+        "prompt": args.prompt,
+        "stages": args.gpus,
+        "parallelism": f"pp{args.gpus}",
+        "l2": "inputs larger than L2: every step streams all weights (16 GB) and the KV caches",
+    }
+
+
+# ---------------------------------------------------------------------------
+# B200 arm, one GPU
+# ---------------------------------------------------------------------------
+
+def run_single(args) -> None:
+    from gpu_mesh_b200 import _lib, build_pipeline, greedy_sample
+    from gpu_mesh_b200.pipeline import pipeline_decode_multi
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = llama3_8b()
+    hbm, tflops, peak_kind = peaks()
+    workers = build_pipeline(cfg, 1, [dev], transport="local_cuda", dtype=torch.bfloat16, check_values=False)
+    w = workers[0]
+    stage = w._model
+    keys = [f"mb{i}" for i in range(args.micro_batches)]
+    cap = args.prompt + args.warmup + 2 * args.steps + 16
+    for k in keys:
+        w.reserve_kv(k, args.micro, cap)
+    g = torch.Generator().manual_seed(1000)
+    prompts = [torch.randint(0, cfg.vocab_size, (args.micro, args.prompt), generator=g) for _ in keys]
+
+    # Prefill every micro-batch (timed for the report, not the headline).
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    first = []
+    for k, p in zip(keys, prompts):
+        logits = w.forward_inference(None, input_ids=p.to(dev), operation_id=1, attempt_id="b",
+                                     cache_key=k, logits="last").output
+        first.append(greedy_sample(logits[:, -1]))
+    t1.record()
+    torch.cuda.synchronize()
+    prefill_ms = t0.elapsed_time(t1)
+    ids = torch.cat(first).unsqueeze(-1)
+
+    def step(ids):
+        logits = w.decode_multi(None, keys, input_ids=ids, logits="last")
+        return greedy_sample(logits[:, -1]).unsqueeze(-1)
+
+    for _ in range(args.warmup):
+        ids = step(ids)
+    torch.cuda.synchronize()
+    launches0 = _lib.lib().mg_launch_count()
+    stage.profile(True)
+    with ClockSampler(0) as clocks:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            ids = step(ids)
+        e1.record()
+        torch.cuda.synchronize()
+    prof = stage.profile_read()
+    stage.profile(False)
+    launches = _lib.lib().mg_launch_count() - launches0
+    ms = e0.elapsed_time(e1)
+    rows = args.micro * args.micro_batches
+    value = rows * args.steps / (ms / 1000.0)
+
+    # End to end through the public API: host ids in, host tokens out, every step.
+    host_ids = ids.cpu().pin_memory()
+    host_out = torch.empty_like(host_ids).pin_memory()
+    torch.cuda.synchronize()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        d_ids = host_ids.to(dev, non_blocking=True)
+        logits = pipeline_decode_multi(workers, d_ids, cache_keys=keys, logits="last")
+        tok = greedy_sample(logits[:, -1]).unsqueeze(-1)
+        host_out.copy_(tok, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        host_ids.copy_(host_out)
+    e3.record()
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3)
+
+    lin = prof["linear_decode"]
+    att = prof["attention"]
+    lin_gbs = lin["bytes"] / (lin["ms"] / 1000.0) / 1e9 if lin["ms"] else 0.0
+    att_gbs = att["bytes"] / (att["ms"] / 1000.0) / 1e9 if att["ms"] else 0.0
+    step_bytes = sum(p["bytes"] for p in prof.values()) / args.steps
+
+    base = None
+    if not args.no_cpu_baseline:
+        base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=2)
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, uniform-random prompt ids)",
+        "config": workload_config(args),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "gemv_mma (decode linear layers, weight streaming)",
+            "achieved": lin_gbs,
+            "peak": hbm,
+            "unit": "GB/s",
+            "frac": lin_gbs / hbm,
+            "traffic": None,
+            "peak_kind": peak_kind,
+            "share_of_step": lin["ms"] / ms if ms else None,
+        },
+        "attention_roofline": {
+            "bound": "hbm",
+            "kernel": "attn_split + combine (decode attention over the stage-owned KV)",
+            "achieved": att_gbs,
+            "peak": hbm,
+            "unit": "GB/s",
+            "frac": att_gbs / hbm,
+            "share_of_step": att["ms"] / ms if ms else None,
+        },
+        "step_roofline": {
+            "bytes_per_step": step_bytes,
+            "achieved_gbs": step_bytes / (ms / args.steps / 1000.0) / 1e9,
+            "frac": step_bytes / (ms / args.steps / 1000.0) / 1e9 / hbm,
+        },
+        "e2e": {
+            "value": rows * args.steps / (e2e_ms / 1000.0),
+            "unit": "tok/s",
+            "h2d_bytes_per_step": rows * 8,
+            "d2h_bytes_per_step": rows * 8,
+        },
+        "prefill": {
+            "tok_s": rows * args.prompt / (prefill_ms / 1000.0),
+            "ms": prefill_ms,
+        },
+        "gpu_launches": int(launches),
+        "profile": prof,
+        "clocks": clocks.summary(),
+    }
+    if base is not None:
+        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--micro", type=int, default=8)
+    ap.add_argument("--micro-batches", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        run_single(args)
+        return
+    from gpu_mesh_b200.dist import run_pipeline_bench
+
+    run_pipeline_bench(args, llama3_8b(), METRIC, workload_config(args), peaks())
+
+
+if __name__ == "__main__":
+    main()

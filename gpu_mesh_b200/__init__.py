@@ -1,0 +1,38 @@
+"""B200-native stage executor for MeshGPU-style pipeline inference.
+
+Dense decoder stages (Llama and Qwen3 architectures) run on hand-written
+sm_100a CUDA kernels behind a C ABI (``include/meshgpu_b200.h``); this package
+is the Python host side with the reference's stage / pipeline API.
+"""
+from gpu_mesh_b200.config import LlamaConfig, config_from, split_layers
+from gpu_mesh_b200.pipeline import (
+    build_pipeline,
+    from_reference_workers,
+    pipeline_decode_step,
+    pipeline_decode_step_async,
+    pipeline_prefill,
+    pipeline_prefill_async,
+)
+from gpu_mesh_b200.sampling import SamplingParams, greedy_sample, make_sampling_generator, top_p_sample
+from gpu_mesh_b200.stage import B200Stage
+from gpu_mesh_b200.stage_worker import B200StageWorker, ForwardResult, StageContext
+
+__all__ = [
+    "B200Stage",
+    "B200StageWorker",
+    "ForwardResult",
+    "LlamaConfig",
+    "SamplingParams",
+    "StageContext",
+    "build_pipeline",
+    "config_from",
+    "from_reference_workers",
+    "greedy_sample",
+    "make_sampling_generator",
+    "pipeline_decode_step",
+    "pipeline_decode_step_async",
+    "pipeline_prefill",
+    "pipeline_prefill_async",
+    "split_layers",
+    "top_p_sample",
+]

@@ -1,0 +1,120 @@
+// Token embedding gather, RMSNorm and KV-slot copies.
+//
+// RMSNorm follows LlamaStage's RMSNorm.forward (models/llama_dense.py:91-93)
+// and HF Qwen3RMSNorm: mean of squares in fp32, multiply by 1/sqrt(ms + eps),
+// round to the activation dtype, then multiply by the weight in that dtype.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mg {
+namespace {
+
+template <typename T>
+__global__ void embed_kernel(const T* __restrict__ table, const int64_t* __restrict__ ids, int H,
+                             int V, T* __restrict__ out, int* err) {
+  const int m = blockIdx.x;
+  int64_t id = ids[m];
+  if (id < 0 || id >= V) {
+    flag_error(err, kErrTokenRange);
+    id = 0;
+  }
+  constexpr int VEC = Vec16<T>::N;
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)m * H);
+  for (int i = threadIdx.x; i < H / VEC; i += blockDim.x) dst[i] = src[i];
+}
+
+template <typename T>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (lane < nw) ? red[lane] : 0.f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __restrict__ w, int H,
+                               float eps, T* __restrict__ y) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const T* xr = x + (size_t)m * xs;
+  T* yr = y + (size_t)m * H;
+  constexpr int VEC = Vec16<T>::N;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H / VEC; i += blockDim.x) {
+    float v[VEC];
+    load16_f<T>(xr + i * VEC, v);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) ss += v[j] * v[j];
+  }
+  ss = block_sum<T>(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)H + eps);
+  for (int i = threadIdx.x; i < H / VEC; i += blockDim.x) {
+    float v[VEC], g[VEC];
+    load16_f<T>(xr + i * VEC, v);
+    load16_f<T>(w + i * VEC, g);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) stf<T>(yr + i * VEC + j, rt<T>(rt<T>(v[j] * r) * g[j]));
+  }
+}
+
+template <typename T>
+__global__ void kv_copy_kernel(T* __restrict__ kv, int layer, int kvsel, int slot_rows, int nkv,
+                               int cap, int D, int len, T* __restrict__ ext, bool to_slot) {
+  // grid: (len, nkv, slot_rows); block covers D.
+  const int pos = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
+  T* sp = kv + kv_offset_elems(layer, kvsel, slot_rows, r, nkv, h, cap, D, pos);
+  T* ep = ext + (((size_t)r * nkv + h) * len + pos) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    if (to_slot) sp[d] = ep[d];
+    else ep[d] = sp[d];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M, int H, int V,
+                         void* out, int* err, cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  if (dtype == kBF16)
+    { embed_kernel<__nv_bfloat16><<<M, 128, 0, s>>>((const __nv_bfloat16*)table, ids, H, V,
+                                                  (__nv_bfloat16*)out, err); note_launch(); }
+  else
+    { embed_kernel<float><<<M, 128, 0, s>>>((const float*)table, ids, H, V, (float*)out, err); note_launch(); }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t xs, const void* w, int M, int H,
+                           float eps, void* y, cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  const int threads = H >= 2048 ? 256 : 128;
+  if (dtype == kBF16)
+    { rmsnorm_kernel<__nv_bfloat16><<<M, threads, 0, s>>>(
+        (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y); note_launch(); }
+  else
+    { rmsnorm_kernel<float><<<M, threads, 0, s>>>((const float*)x, xs, (const float*)w, H, eps,
+                                                (float*)y); note_launch(); }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kv_copy(int dtype, void* kv_base, int layer, int kv, int slot_rows, int nkv,
+                           int cap, int D, int len, void* ext, bool to_slot, cudaStream_t s) {
+  if (len == 0) return cudaSuccess;
+  dim3 grid(len, nkv, slot_rows);
+  const int threads = D < 128 ? D : 128;
+  if (dtype == kBF16)
+    { kv_copy_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>((__nv_bfloat16*)kv_base, layer, kv,
+                                                           slot_rows, nkv, cap, D, len,
+                                                           (__nv_bfloat16*)ext, to_slot); note_launch(); }
+  else
+    { kv_copy_kernel<float><<<grid, threads, 0, s>>>((float*)kv_base, layer, kv, slot_rows, nkv, cap,
+                                                   D, len, (float*)ext, to_slot); note_launch(); }
+  return cudaGetLastError();
+}
+
+}  // namespace mg

@@ -1,0 +1,92 @@
+// QKV post-processing: per-head QK-norm (Qwen3), rotary embedding, and the
+// in-place KV-cache append.
+//
+// The reference grows its cache with torch.cat every step
+// (models/llama_dense.py:166-170), copying all past K/V.  Here the slot is
+// preallocated and each forward writes only its new positions.  RoPE follows
+// _apply_rope (llama_dense.py:112-125) with tables already cast to the
+// activation dtype (:431-432): y = round(round(x*cos) + round(rotate_half(x)*sin)).
+// QK-norm follows HF Qwen3Attention (q_norm/k_norm over head_dim before RoPE).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mg {
+namespace {
+
+constexpr int kHeadsPerCta = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_kernel(QkvPostArgs a) {
+  __shared__ float xs[kHeadsPerCta][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x;
+  const int hh = blockIdx.y * kHeadsPerCta + warp;
+  const int nh = a.nq + 2 * a.nkv;
+  if (hh >= nh) return;
+  const int D = a.D, half = D / 2;
+  const int b = m / a.S, s = m % a.S;
+  const RowDesc rd = a.rows[b];
+  const int cache_pos = rd.past + s;
+  int64_t pos = a.positions ? a.positions[m] : (int64_t)cache_pos;
+  if (pos < 0 || pos >= a.max_pos) {
+    flag_error(a.err, kErrPositionRange);
+    pos = pos < 0 ? 0 : a.max_pos - 1;
+  }
+
+  const T* src = (const T*)a.qkv + (size_t)m * nh * D + (size_t)hh * D;
+  float* x = xs[warp];
+  for (int d = lane; d < D; d += 32) x[d] = ldf<T>(src + d);
+  __syncwarp();
+
+  const bool is_q = hh < a.nq;
+  const bool is_k = !is_q && hh < a.nq + a.nkv;
+  T* kv = (T*)rd.kv_base;
+
+  if (!is_q && !is_k) {  // value head: plain append
+    const int h = hh - a.nq - a.nkv;
+    T* dst = kv + kv_offset_elems(a.layer, 1, rd.slot_rows, rd.row, a.nkv, h, rd.cap, D, cache_pos);
+    for (int d = lane; d < D; d += 32) stf<T>(dst + d, x[d]);
+    return;
+  }
+
+  const T* nw = is_q ? (const T*)a.q_norm : (const T*)a.k_norm;
+  if (nw) {
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) ss += x[d] * x[d];
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)D + a.eps);
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) x[d] = rt<T>(rt<T>(x[d] * r) * ldf<T>(nw + d));
+    __syncwarp();
+  }
+
+  const T* cs = (const T*)a.cos + (size_t)pos * half;
+  const T* sn = (const T*)a.sin + (size_t)pos * half;
+  T* dst;
+  if (is_q) {
+    dst = (T*)a.q_out + ((size_t)m * a.nq + hh) * D;
+  } else {
+    const int h = hh - a.nq;
+    dst = kv + kv_offset_elems(a.layer, 0, rd.slot_rows, rd.row, a.nkv, h, rd.cap, D, cache_pos);
+  }
+  for (int d = lane; d < D; d += 32) {
+    const float c = ldf<T>(cs + (d % half)), sv = ldf<T>(sn + (d % half));
+    const float rot = d < half ? -x[d + half] : x[d - half];
+    stf<T>(dst + d, rt<T>(x[d] * c) + rt<T>(rot * sv));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
+  const int M = a.B * a.S;
+  if (M == 0) return cudaSuccess;
+  dim3 grid(M, (a.nq + 2 * a.nkv + kHeadsPerCta - 1) / kHeadsPerCta);
+  if (a.dtype == kBF16)
+    { qkv_post_kernel<__nv_bfloat16><<<grid, kHeadsPerCta * 32, 0, s>>>(a); note_launch(); }
+  else
+    { qkv_post_kernel<float><<<grid, kHeadsPerCta * 32, 0, s>>>(a); note_launch(); }
+  return cudaGetLastError();
+}
+
+}  // namespace mg

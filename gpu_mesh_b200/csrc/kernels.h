@@ -1,0 +1,108 @@
+// Host-side launchers of the stage kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mg {
+
+// Count `n` kernel launches (process-wide, read by mg_launch_count).
+void note_launch(int n = 1);
+
+// One sequence row of a forward batch: where its KV cache lives and how long
+// it was before this forward.  Kept in device memory so that a captured decode
+// step reads the current lengths instead of baking them in.
+struct RowDesc {
+  uint64_t kv_base;   // device address of the slot's KV block
+  int32_t slot_rows;  // rows (batch) of the slot
+  int32_t row;        // this row's index inside the slot
+  int32_t cap;        // positions the slot can hold
+  int32_t past;       // cached positions before this forward
+};
+
+// KV block layout of a slot: [local_layer][2 (K,V)][slot_rows][nkv][cap][D].
+__host__ __device__ inline size_t kv_offset_elems(int layer, int kv, int slot_rows, int row,
+                                                  int nkv, int head, int cap, int D, int pos) {
+  return ((((size_t)(layer * 2 + kv) * slot_rows + row) * nkv + head) * cap + pos) * D;
+}
+
+// Linear epilogues: Y = f(X · Wᵀ).
+enum Epilogue : int {
+  kEpiStore = 0,   // Y = round(acc)
+  kEpiResid = 1,   // Y = round(R + round(acc))            (o_proj / down_proj + residual)
+  kEpiSwiGLU = 2,  // Y[:, n] = round(round(silu(round(acc_gate))) * round(acc_up))
+};
+
+// Attention mask policies.
+enum MaskPolicy : int {
+  kMaskSdpa = 0,         // Llama sdpa: single-token query sees every key; else key j <= position
+  kMaskEager = 1,        // Llama eager: key j <= position
+  kMaskCacheCausal = 2,  // HF causal mask: key j <= past + s
+};
+
+struct LinearArgs {
+  int dtype;
+  const void* X; int64_t ldx;   // [M, K], row stride ldx elements
+  const void* W;                // [N, K] (kEpiSwiGLU: [2*N, K], gate rows then up rows)
+  void* Y; int64_t ldy;         // [M, N]
+  const void* R; int64_t ldr;   // residual for kEpiResid (may alias Y)
+  int M, N, K;
+  int epilogue;
+  float* partial;               // split-K scratch, fp32
+  size_t partial_elems;         // capacity of `partial`
+};
+
+// Scratch (fp32 elements) that launch_linear needs for the given shape.
+size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue);
+cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s);
+
+cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M, int H, int V,
+                         void* out, int* err, cudaStream_t s);
+
+// y[m] = RMSNorm(x[m * x_row_stride]) for m < M.
+cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t x_row_stride, const void* w, int M,
+                           int H, float eps, void* y, cudaStream_t s);
+
+struct QkvPostArgs {
+  int dtype;
+  const void* qkv;         // [M, (nq + 2 nkv) * D]
+  const int64_t* positions;// [M] or NULL (position = past + s)
+  const RowDesc* rows;     // [B]
+  const void* q_norm;      // [D] or NULL
+  const void* k_norm;      // [D] or NULL
+  const void* cos;         // [max_pos, D/2]
+  const void* sin;
+  void* q_out;             // [M, nq, D]
+  int* err;
+  int B, S, nq, nkv, D, layer, max_pos;
+  float eps;
+};
+cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t s);
+
+struct AttnArgs {
+  int dtype;
+  const void* q;            // [M, nq, D]
+  const int64_t* positions; // [M] or NULL
+  const RowDesc* rows;      // [B]
+  void* out;                // [M, nq, D]
+  float* partial;           // split scratch
+  size_t partial_elems;
+  int B, S, nq, nkv, D, layer, mask;
+  int max_keys;             // upper bound of keys any row can see (past + S)
+  float scale;
+};
+size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+cudaError_t launch_argmax(int dtype, const void* logits, int rows, int vocab, int64_t row_stride,
+                          int64_t* ids, cudaStream_t s);
+cudaError_t launch_top_p(int dtype, const void* logits, int rows, int vocab, int64_t row_stride,
+                         float temperature, float top_p, const float* uniforms, int64_t* ids,
+                         cudaStream_t s);
+
+// Copy [slot_rows, nkv, len, D] K or V of one layer in or out of a slot.
+cudaError_t launch_kv_copy(int dtype, void* kv_base, int layer, int kv, int slot_rows, int nkv,
+                           int cap, int D, int len, void* ext, bool to_slot, cudaStream_t s);
+
+}  // namespace mg

@@ -1,0 +1,212 @@
+"""Host-side logic that needs no GPU: config validation, layer splits, stage
+context, synthetic weights, RoPE tables, and the pipeline coordinator's
+protocol (sync check, rollback, async drain) driven with fake workers.
+
+Mirrors the reference's unit tests (tests/unit/test_model.py:39-61,
+tests/unit/test_inference.py:196-233 rollback, :39-61 drain)."""
+from __future__ import annotations
+
+import asyncio
+import threading
+
+import pytest
+import torch
+
+from gpu_mesh_b200 import pipeline as P
+from gpu_mesh_b200.config import LlamaConfig, config_from, split_layers
+from gpu_mesh_b200.sampling import SamplingParams, make_sampling_generator
+from gpu_mesh_b200.stage_worker import StageContext
+from gpu_mesh_b200.weights import (
+    rope_tables,
+    slice_stage_state,
+    synthetic_model_state,
+    synthetic_stage_state,
+)
+
+TINY = dict(
+    vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=4,
+    num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=64,
+)
+
+
+def test_config_rejects_invalid_numeric_values():
+    with pytest.raises(TypeError, match="num_hidden_layers"):
+        LlamaConfig(**{**TINY, "num_hidden_layers": 2.0})
+    with pytest.raises(ValueError, match="rms_norm_eps"):
+        LlamaConfig(**TINY, rms_norm_eps=float("nan"))
+    with pytest.raises(ValueError, match="divisible"):
+        LlamaConfig(**{**TINY, "num_attention_heads": 3})
+    with pytest.raises(ValueError, match="even"):
+        LlamaConfig(**{**TINY, "head_dim": 15})
+    with pytest.raises(ValueError, match="attention_implementation"):
+        LlamaConfig(**TINY, attention_implementation="flash")
+
+
+def test_config_from_hf_qwen3():
+    from transformers import Qwen3Config
+
+    hf = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+                     max_position_embeddings=128, tie_word_embeddings=True,
+                     rope_parameters={"rope_type": "default", "rope_theta": 1e6})
+    cfg = config_from(hf)
+    assert cfg.qk_norm and cfg.mask_policy == "cache" and cfg.tie_word_embeddings
+    assert cfg.rope_theta == 1e6 and cfg.head_dim == 32 and cfg.rms_norm_eps == hf.rms_norm_eps
+
+
+def test_split_layers_matches_reference_rule():
+    assert split_layers(32, 1) == [(0, 32)]
+    assert split_layers(22, 4) == [(0, 6), (6, 12), (12, 17), (17, 22)]
+    assert split_layers(36, 8)[0] == (0, 5) and split_layers(36, 8)[-1] == (32, 36)
+    with pytest.raises(ValueError):
+        split_layers(4, 5)
+
+
+def test_stage_context_validation():
+    with pytest.raises(ValueError, match="non-empty layer range"):
+        StageContext(0, 2, 2, "cpu", True, True, "j", "a")
+    with pytest.raises(ValueError, match="transport"):
+        StageContext(0, 0, 2, "cpu", True, True, "j", "a", transport="tcp")
+    with pytest.raises(TypeError):
+        StageContext(True, 0, 2, "cpu", True, True, "j", "a")
+
+
+def test_synthetic_weights_are_sliceable_and_deterministic():
+    cfg = LlamaConfig(**TINY)
+    full = synthetic_model_state(cfg, seed=3)
+    again = synthetic_model_state(cfg, seed=3)
+    assert all(torch.equal(full[k], again[k]) for k in full)
+    stage = synthetic_stage_state(cfg, 2, 4, has_embedding=False, has_lm_head=True, seed=3)
+    cut = slice_stage_state(full, 2, 4, has_embedding=False, has_lm_head=True)
+    assert stage.keys() == cut.keys()
+    assert all(torch.equal(stage[k], cut[k]) for k in stage)
+    w = full["layers.0.self_attn.q_proj.weight"]
+    assert abs(float(w.std()) - 0.02) < 2e-3 and torch.all(full["norm.weight"] == 1)
+
+
+def test_tied_lm_head_is_the_embedding():
+    cfg = LlamaConfig(**TINY, tie_word_embeddings=True)
+    sd = synthetic_stage_state(cfg, 0, 4, has_embedding=True, has_lm_head=True)
+    assert sd["lm_head.weight"] is sd["embed_tokens.weight"]
+
+
+def test_rope_tables_match_hf_qwen3_rotary_embedding():
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+
+    hf = Qwen3Config(head_dim=128, hidden_size=256, num_attention_heads=2, max_position_embeddings=64,
+                     rope_parameters={"rope_type": "default", "rope_theta": 1e6})
+    emb = Qwen3RotaryEmbedding(hf)
+    pos = torch.arange(64).unsqueeze(0)
+    cos_hf, sin_hf = emb(torch.zeros(1, dtype=torch.bfloat16), pos)
+    cos, sin = rope_tables(128, 64, 1e6, torch.bfloat16)
+    assert torch.equal(cos_hf[0, :, :64], cos) and torch.equal(sin_hf[0, :, :64], sin)
+
+
+def test_sampling_params_validation():
+    with pytest.raises(ValueError, match="temperature"):
+        SamplingParams(temperature=-1)
+    with pytest.raises(ValueError, match="top_p"):
+        SamplingParams(top_p=1.5)
+    with pytest.raises(TypeError):
+        SamplingParams(seed=1.5)
+    assert make_sampling_generator(SamplingParams()) is None
+    g1 = make_sampling_generator(SamplingParams(seed=5))
+    g2 = make_sampling_generator(SamplingParams(seed=5))
+    assert torch.equal(torch.rand(3, generator=g1), torch.rand(3, generator=g2))
+
+
+# ---------------------------------------------------------------------------
+# Coordinator protocol with fake workers (no GPU).
+# ---------------------------------------------------------------------------
+
+class FakeWorker:
+    """Records calls and keeps a per-key length like a stage would."""
+
+    def __init__(self, name, fail_on=None, delay_event=None):
+        self.name = name
+        self.len = {}
+        self.fail_on = fail_on
+        self.calls = []
+        self.delay_event = delay_event
+
+    def clear_kv(self, key=None):
+        self.calls.append(("clear", key))
+        self.len.pop(key, None)
+
+    def kv_cache_length(self, key=None):
+        return self.len.get(key, 0)
+
+    def trim_kv(self, length, key=None):
+        self.calls.append(("trim", key, length))
+        self.len[key] = length
+
+    def forward_inference(self, hidden, *, input_ids=None, position_ids=None, operation_id, attempt_id,
+                          reset_kv=False, cache_key=None, attention_mask=None):
+        if self.delay_event is not None:
+            self.delay_event.wait(5)
+        src = input_ids if input_ids is not None else hidden
+        self.len[cache_key] = self.len.get(cache_key, 0) + src.shape[1]
+        self.calls.append(("fwd", cache_key, None if position_ids is None else position_ids[0].tolist()))
+        if self.fail_on == operation_id:
+            raise RuntimeError(f"{self.name} failed")
+
+        class R:
+            output = torch.zeros(src.shape[0], src.shape[1], 4)
+
+        return R()
+
+
+def test_decode_checks_sync_and_prefill():
+    a, b = FakeWorker("a"), FakeWorker("b")
+    with pytest.raises(RuntimeError, match="requires a prefilled KV cache"):
+        P.pipeline_decode_step([a, b], torch.zeros(1, 1, dtype=torch.long), operation_id=2)
+    a.len[None], b.len[None] = 3, 2
+    with pytest.raises(RuntimeError, match="out of sync"):
+        P.pipeline_decode_step([a, b], torch.zeros(1, 1, dtype=torch.long), operation_id=2)
+
+
+def test_decode_feeds_positions_and_rolls_back_on_failure():
+    a, b = FakeWorker("a"), FakeWorker("b", fail_on=3)
+    ids = torch.zeros(1, 4, dtype=torch.long)
+    P.pipeline_prefill([a, b], ids, cache_key="k")
+    P.pipeline_decode_step([a, b], torch.zeros(1, 2, dtype=torch.long), operation_id=2, cache_key="k")
+    assert a.calls[-1] == ("fwd", "k", [4, 5])
+    with pytest.raises(RuntimeError, match="b failed"):
+        P.pipeline_decode_step([a, b], torch.zeros(1, 1, dtype=torch.long), operation_id=3, cache_key="k")
+    assert a.len["k"] == 6 and b.len["k"] == 6  # trimmed back to the pre-step lengths
+    assert ("trim", "k", 6) in a.calls
+
+
+def test_prefill_failure_clears_every_stage():
+    a, b = FakeWorker("a"), FakeWorker("b", fail_on=1)
+    with pytest.raises(RuntimeError):
+        P.pipeline_prefill([a, b], torch.zeros(1, 4, dtype=torch.long), cache_key="k")
+    assert a.kv_cache_length("k") == 0 and b.kv_cache_length("k") == 0
+
+
+def test_prefill_rejects_bad_shapes():
+    with pytest.raises(ValueError, match="batch, sequence"):
+        P.pipeline_prefill([FakeWorker("a")], torch.zeros(4, dtype=torch.long))
+    with pytest.raises(ValueError, match="non-empty"):
+        P.pipeline_prefill([FakeWorker("a")], torch.zeros(1, 0, dtype=torch.long))
+    with pytest.raises(ValueError, match="workers"):
+        P.pipeline_prefill([], torch.zeros(1, 2, dtype=torch.long))
+
+
+def test_async_call_drains_on_cancel():
+    gate = threading.Event()
+    w = FakeWorker("slow", delay_event=gate)
+
+    async def main():
+        task = asyncio.create_task(P.pipeline_prefill_async([w], torch.zeros(1, 2, dtype=torch.long)))
+        await asyncio.sleep(0.05)
+        task.cancel()
+        await asyncio.sleep(0.05)
+        gate.set()
+        with pytest.raises(asyncio.CancelledError):
+            await task
+
+    asyncio.run(main())
+    # the running stage call finished before cancellation propagated
+    assert any(c[0] == "fwd" for c in w.calls)
