@@ -182,3 +182,10 @@ def check(status: int) -> None:
     if status == MG_EDEVICE:
         raise DeviceRangeError(msg)
     raise MeshGpuError(msg)
+
+
+SIGNATURES["mg_linear"] = (
+    ctypes.c_int,
+    [_i32, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, ctypes.c_uint64, _vp],
+)
+SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i32])

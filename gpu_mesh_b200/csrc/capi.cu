@@ -402,6 +402,7 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   la.dtype = dt;
   la.partial = st->part;
   la.partial_elems = st->work_scratch;
+  la.err = st->err;
   la.M = M;
 
   QkvPostArgs qa{};
@@ -884,6 +885,35 @@ int mg_stage_profile_read(mg_stage* st, mg_profile* out) {
 }
 
 uint64_t mg_launch_count(void) { return g_launches.load(); }
+
+uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32_t epilogue) {
+  return linear_scratch_elems(dtype, M, N, K, epilogue);
+}
+
+int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t M, int32_t N,
+              int32_t K, int32_t epilogue, const void* R, int64_t ldr, void* Y, int64_t ldy,
+              float* scratch, uint64_t scratch_elems, void* stream) {
+  if (!X || !W || !Y || M < 0 || N < 1 || K < 1) return fail(MG_EINVAL, "invalid linear arguments");
+  if (dtype != MG_DTYPE_F32 && dtype != MG_DTYPE_BF16) return fail(MG_EINVAL, "invalid dtype");
+  if (epilogue < MG_EPI_STORE || epilogue > MG_EPI_SWIGLU) return fail(MG_EINVAL, "invalid epilogue");
+  if (epilogue == MG_EPI_RESID && !R) return fail(MG_EINVAL, "the residual epilogue needs R");
+  if (ldx < K || ldy < N || (R && ldr < N)) return fail(MG_EINVAL, "leading dimensions too small");
+  const int vec = dtype == MG_DTYPE_BF16 ? 8 : 4;
+  if (K % vec || N % vec || ldx % vec || ldy % vec || (R && ldr % vec))
+    return fail(MG_EINVAL, "K, N and leading dimensions must be multiples of 16 bytes");
+  if (linear_scratch_elems(dtype, M, N, K, epilogue) > scratch_elems)
+    return fail(MG_EINVAL, "scratch too small: %llu fp32 elements needed",
+                (unsigned long long)linear_scratch_elems(dtype, M, N, K, epilogue));
+  LinearArgs la{};
+  la.dtype = dtype;
+  la.X = X; la.ldx = ldx; la.W = W; la.Y = Y; la.ldy = ldy; la.R = R; la.ldr = ldr;
+  la.M = M; la.N = N; la.K = K; la.epilogue = epilogue;
+  la.partial = scratch;
+  la.partial_elems = scratch_elems;
+  la.err = nullptr;
+  MG_LAUNCH(launch_linear(la, (cudaStream_t)stream), "linear");
+  return MG_OK;
+}
 
 int mg_sample_greedy(const void* logits, int32_t dtype, int32_t rows, int32_t vocab,
                      int64_t row_stride, int64_t* ids, void* stream) {

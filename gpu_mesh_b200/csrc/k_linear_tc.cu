@@ -1,10 +1,355 @@
-// Prefill GEMM on tcgen05 (placeholder until the TMEM kernel lands).
+// Prefill GEMM on the 5th-generation tensor cores: Y = epilogue(X · Wᵀ).
+//
+// X [M, K] and W [N, K] are both K-major (nn.Linear layout), so one CTA
+// computes a 128 x BN output tile as
+//   * warp 0, one lane: TMA producer — cp.async.bulk.tensor 2-D loads of a
+//     128 x 64 X tile and BN/128 W tiles of 128 x 64 per K block, 128-byte
+//     swizzle, into a STAGES-deep ring guarded by mbarriers (no multicast);
+//   * warp 1, one lane: MMA issuer — four tcgen05.mma (M=128, N=BN, K=16)
+//     per K block with the fp32 accumulator in TMEM; tcgen05.commit releases
+//     each smem stage and finally signals the epilogue;
+//   * all four warps: epilogue — tcgen05.ld of their 32 TMEM lanes (rows),
+//     rounding to bf16 with the reference's rounding points, residual add or
+//     SwiGLU, 16-byte global stores.
+// For SwiGLU the BN = 256 tile is 128 gate rows followed by the matching 128
+// up rows, so each thread holds gate and up of the same output column.
+// Every mbarrier wait is bounded (about two seconds of %globaltimer); on
+// expiry the kernel records kErrTimeout in the stage's error word, skips the
+// remaining work, frees its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
 #include "linear_tc.h"
 
 namespace mg {
+namespace {
 
-bool linear_tc_applicable(int, int, int, int) { return false; }
+using bf16 = __nv_bfloat16;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes: one swizzle atom row
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and the stage error word set) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) {
+      if (err) atomicCAS(err, 0, 3);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: bf16 x bf16 -> fp32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t instr_desc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+template <int BN>
+struct TcSmem {
+  static constexpr int kA = kBM * kBK * 2;     // bytes per A stage
+  static constexpr int kB = BN * kBK * 2;      // bytes per B stage
+  static constexpr int kTiles = kStages * (kA + kB);
+  static constexpr int kBytes = kTiles + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   LinearArgs a, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  using L = TcSmem<BN>;
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kStages * L::kA;
+  uint64_t* full = (uint64_t*)(smem + L::kTiles);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_holder = (uint32_t*)(acc_full + 1);
+  int* abort_flag = (int*)(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM;
+  const int n0 = (EPI == kEpiSwiGLU) ? blockIdx.x * (BN / 2) : blockIdx.x * BN;
+  const int nk = (a.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+
+  int issued = 0;
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages, round = kb / kStages;
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, err)) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      if (*(volatile int*)abort_flag) break;
+      mbar_expect_tx(&full[s], L::kA + L::kB);
+      tma_load_2d(sa + s * L::kA, &tm_x, &full[s], kb * kBK, m0);
+#pragma unroll
+      for (int j = 0; j < BN / 128; ++j) {
+        const int row = (EPI == kEpiSwiGLU) ? (j == 0 ? n0 : a.N + n0) : n0 + 128 * j;
+        tma_load_2d(sb + s * L::kB + j * 128 * kBK * 2, &tm_w, &full[s], kb * kBK, row);
+      }
+      issued = kb + 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    constexpr uint32_t idesc = instr_desc(BN);
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages, round = kb / kStages;
+      if (!mbar_wait(&full[s], round & 1, err)) {
+        *(volatile int*)abort_flag = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t da = smem_desc(sa + s * L::kA);
+      const uint64_t db = smem_desc(sb + s * L::kB);
+#pragma unroll
+      for (int j = 0; j < kBK / 16; ++j)
+        mma_bf16(tmem, da + 2 * j, db + 2 * j, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+      mma_commit(&empty[s]);
+    }
+    (void)ok;
+    // Arrives once every MMA issued above has finished (immediately if none).
+    mma_commit(acc_full);
+  }
+  __syncwarp();
+
+  // Epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w+31.
+  const bool have = mbar_wait(acc_full, 0, err) && !*(volatile int*)abort_flag;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  constexpr int NOUT = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  if (have) {
+#pragma unroll 1
+    for (int c = 0; c < NOUT; c += 32) {
+      float v[32], u[32];
+      tmem_ld32(trow + c, v);
+      if (EPI == kEpiSwiGLU) tmem_ld32(trow + BN / 2 + c, u);
+      const int n = n0 + c;
+      if (row >= a.M || n >= a.N) continue;
+      bf16* y = (bf16*)a.Y + (size_t)row * a.ldy + n;
+      const int cols = min(32, a.N - n);  // multiple of 16 by the applicability check
+      if (EPI == kEpiResid) {
+        const bf16* r = (const bf16*)a.R + (size_t)row * a.ldr + n;
+        for (int i = 0; i < cols; i += 8) {
+          float rv[8];
+          load16_f<bf16>(r + i, rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[i + e] = rv[e] + rt<bf16>(v[i + e]);
+        }
+      } else if (EPI == kEpiSwiGLU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float g = rt<bf16>(v[i]), up = rt<bf16>(u[i]);
+          v[i] = rt<bf16>(g / (1.0f + expf(-g))) * up;
+        }
+      }
+      for (int i = 0; i < cols; i += 8) {
+        uint4 o;
+        o.x = pack_bf16(v[i + 0], v[i + 1]);
+        o.y = pack_bf16(v[i + 2], v[i + 3]);
+        o.z = pack_bf16(v[i + 4], v[i + 5]);
+        o.w = pack_bf16(v[i + 6], v[i + 7]);
+        *reinterpret_cast<uint4*>(y + i) = o;
+      }
+    }
+  }
+  if (warp == 0 && lane == 0 && *(volatile int*)abort_flag) {
+    // After a timeout, let the loads this CTA issued land before it exits.
+    for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+      mbar_wait(&full[kb % kStages], (kb / kStages) & 1, err);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiled)p;
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box 128 rows x 64 cols.
+bool make_map(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {kBK, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_tc(const LinearArgs& a, cudaStream_t s) {
+  CUtensorMap tx, tw;
+  const uint64_t wrows = (EPI == kEpiSwiGLU) ? 2ull * a.N : (uint64_t)a.N;
+  if (!make_map(&tx, a.X, a.M, a.K, a.ldx) || !make_map(&tw, a.W, wrows, a.K, a.K))
+    return cudaErrorInvalidValue;
+  constexpr int smem = TcSmem<BN>::kBytes;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int ntile = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  dim3 grid((a.N + ntile - 1) / ntile, (a.M + kBM - 1) / kBM);
+  { gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, s>>>(tx, tw, a, a.err); note_launch(); }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool linear_tc_applicable(int dtype, int M, int N, int K) {
+  return dtype == kBF16 && M > 32 && N % 16 == 0 && K % kBK == 0 && encoder() != nullptr;
+}
+
 size_t linear_tc_scratch_elems(int, int, int, int) { return 0; }
-cudaError_t launch_linear_tc(const LinearArgs&, cudaStream_t) { return cudaErrorNotSupported; }
+
+cudaError_t launch_linear_tc(const LinearArgs& a, cudaStream_t s) {
+  if (((uintptr_t)a.X % 16) || ((uintptr_t)a.W % 16) || (a.ldx % 8)) return cudaErrorInvalidValue;
+  switch (a.epilogue) {
+    case kEpiStore: return launch_tc<256, kEpiStore>(a, s);
+    case kEpiResid: return launch_tc<256, kEpiResid>(a, s);
+    default: return launch_tc<256, kEpiSwiGLU>(a, s);
+  }
+}
 
 }  // namespace mg

@@ -51,6 +51,7 @@ struct LinearArgs {
   int epilogue;
   float* partial;               // split-K scratch, fp32
   size_t partial_elems;         // capacity of `partial`
+  int* err;                     // stage error word (bounded-wait timeouts)
 };
 
 // Scratch (fp32 elements) that launch_linear needs for the given shape.

@@ -200,6 +200,24 @@ int mg_stage_decode_multi(mg_stage* stage, const int32_t* slots, int32_t n_slots
  * id or position since the last check. */
 int mg_stage_check_device(mg_stage* stage, void* stream);
 
+/* ---- Single linear layer (the stage's GEMM paths: weight-streaming GEMV
+ * for <= 32 rows, tcgen05 GEMM above, SIMT for fp32) ---- */
+
+#define MG_EPI_STORE 0  /* Y = round(X·Wᵀ)                                     */
+#define MG_EPI_RESID 1  /* Y = round(R + round(X·Wᵀ))   (o_proj / down_proj)     */
+#define MG_EPI_SWIGLU 2 /* W = [gate; up] ([2N, K]); Y = round(round(silu(round(g))) * round(u)) */
+
+/* Y[M, N] = epilogue(X[M, K] · W[N, K]ᵀ) in `dtype`, the nn.Linear of the
+ * reference (llama_dense.py:140-143, 239-244) with its rounding points.
+ * `scratch` (fp32, `scratch_elems` elements) serves the split-K GEMV; the
+ * bytes it needs are returned by mg_linear_scratch.  R may alias Y. */
+int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t M, int32_t N,
+              int32_t K, int32_t epilogue, const void* R, int64_t ldr, void* Y, int64_t ldy,
+              float* scratch, uint64_t scratch_elems, void* stream);
+
+/* fp32 scratch elements mg_linear needs for this shape. */
+uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32_t epilogue);
+
 /* ---- Instrumentation (no counterpart in the reference, which has no
  * kernels of its own; used by the benchmark to report roofline fractions) ---- */
 

@@ -80,14 +80,35 @@ def attention(cfg, q, k, v, allowed) -> torch.Tensor:
             scores = scores.masked_fill(~allowed.unsqueeze(1), torch.finfo(q.dtype).min)
         p = torch.softmax(scores.float(), dim=-1).to(q.dtype)
         return torch.matmul(p, vv)
-    scores = torch.matmul(q.float(), kk.float().transpose(2, 3)) * (1.0 / math.sqrt(D))
+    acc = torch.float64 if _EXACT[-1] else torch.float32
+    scores = torch.matmul(q.to(acc), kk.to(acc).transpose(2, 3)) * (1.0 / math.sqrt(D))
     if allowed is not None:
         scores = scores.masked_fill(~allowed.unsqueeze(1), float("-inf"))
     p = torch.softmax(scores, dim=-1)
-    return torch.matmul(p, vv.float()).to(q.dtype)
+    return torch.matmul(p, vv.to(acc)).to(q.dtype)
+
+
+_EXACT = [False]
+
+
+class exact_rounding:
+    """Within this context the oracle accumulates matmuls and attention in
+    float64 and rounds once to the activation dtype at the reference's
+    rounding points: the exactly-rounded computation that any fp32 or bf16
+    implementation (the reference's CPU path included) approximates."""
+
+    def __enter__(self):
+        _EXACT.append(True)
+        return self
+
+    def __exit__(self, *exc):
+        _EXACT.pop()
 
 
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """nn.Linear without bias (llama_dense.py:140-143, 239-241)."""
+    if _EXACT[-1]:
+        return torch.nn.functional.linear(x.double(), w.double()).to(x.dtype)
     return torch.nn.functional.linear(x, w)
 
 

@@ -1,0 +1,108 @@
+"""Single-kernel numerics: the stage's linear layer (``mg_linear``) on each of
+its paths against a plain PyTorch fp32 reference of the same op.
+
+Paths: the weight-streaming GEMV (bf16, <= 32 rows, with and without split-K),
+the tcgen05 GEMM (bf16, > 32 rows) and the SIMT kernel (fp32).
+
+Tolerances: the reference applies the same rounding points (round the
+product to bf16; round again after the residual add; round gate, up,
+silu(gate) and the product for SwiGLU) to an fp32 accumulation.  Two fp32
+accumulations in different orders differ by ~1e-6 relative, which can move a
+bf16 rounding by one unit in the last place, so the bar is 1 ulp for a plain
+product, 2 ulp after a residual add and 3 ulp through SwiGLU.  fp32: 1e-5
+relative to the output's largest magnitude.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gpu_mesh_b200.kernels import linear
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def bf16_ulp(t: torch.Tensor) -> torch.Tensor:
+    a = t.float().abs().clamp(min=2.0**-100)
+    return torch.exp2(torch.floor(torch.log2(a)) - 7)
+
+
+def reference(x, w, epilogue, residual=None):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    rt = (lambda v: v.to(x.dtype).float())
+    if epilogue == "swiglu":
+        n = w.shape[0] // 2
+        g = rt(x.float() @ w[:n].float().T)
+        u = rt(x.float() @ w[n:].float().T)
+        return rt(rt(g / (1 + torch.exp(-g))) * u)
+    acc = x.float() @ w.float().T
+    if epilogue == "resid":
+        return rt(residual.float() + rt(acc))
+    return rt(acc)
+
+
+def check(y, ref, dtype, ulps):
+    if dtype == torch.float32:
+        assert (y.float() - ref).abs().max() <= 1e-5 * ref.abs().max()
+        return
+    err = (y.float() - ref).abs() / bf16_ulp(ref)
+    bad = err > ulps
+    assert not bad.any(), f"{int(bad.sum())} elements beyond {ulps} ulp (max {float(err.max()):.2f})"
+
+
+SHAPES = [
+    # (M, N, K): decode GEMV shapes (split-K when N is narrow) ...
+    (1, 4096, 4096), (5, 6144, 4096), (8, 4096, 14336), (16, 28672 // 2, 4096), (17, 512, 1408),
+    (32, 128256, 4096), (32, 4096, 4096),
+    # ... and prefill shapes on the tcgen05 GEMM, including ragged M.
+    (33, 4096, 4096), (100, 688, 256), (128, 6144, 4096), (300, 4096, 14336), (1024, 1024, 2560),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("epilogue", ["store", "resid", "swiglu"])
+def test_linear_bf16_matches_fp32_reference(M, N, K, epilogue):
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + N + K)
+    x = (torch.randn(M, K, generator=g, device=DEV) * 1.0).to(torch.bfloat16)
+    rows = 2 * N if epilogue == "swiglu" else N
+    w = (torch.randn(rows, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    r = torch.randn(M, N, generator=g, device=DEV).to(torch.bfloat16) if epilogue == "resid" else None
+    ref = reference(x, w, epilogue, r)
+    y = linear(x, w, epilogue=epilogue, residual=None if r is None else r.clone(),
+               out=None if r is None else r.clone())
+    torch.cuda.synchronize()
+    check(y, ref, torch.bfloat16, {"store": 1, "resid": 2, "swiglu": 3}[epilogue])
+
+
+def test_linear_in_place_residual():
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(64, 512, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(256, 512, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    r = torch.randn(64, 256, generator=g, device=DEV).to(torch.bfloat16)
+    ref = reference(x, w, "resid", r)
+    linear(x, w, epilogue="resid", residual=r, out=r)  # Y aliases R, as in the stage
+    check(r, ref, torch.bfloat16, 2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 1408, 512), (64, 512, 1408), (200, 96, 40)])
+@pytest.mark.parametrize("epilogue", ["store", "resid", "swiglu"])
+def test_linear_fp32_matches_reference(M, N, K, epilogue):
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g, device=DEV)
+    rows = 2 * N if epilogue == "swiglu" else N
+    w = torch.randn(rows, K, generator=g, device=DEV) * 0.02
+    r = torch.randn(M, N, generator=g, device=DEV) if epilogue == "resid" else None
+    ref = reference(x, w, epilogue, r)
+    y = linear(x, w, epilogue=epilogue, residual=r)
+    check(y, ref, torch.float32, 0)
+
+
+def test_linear_rejects_bad_arguments():
+    x = torch.zeros(4, 60, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(64, 60, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError, match="multiples of 16 bytes"):
+        linear(x, w)
+    with pytest.raises(ValueError, match="residual"):
+        linear(torch.zeros(4, 64, dtype=torch.bfloat16, device=DEV),
+               torch.zeros(64, 64, dtype=torch.bfloat16, device=DEV), epilogue="resid")
