@@ -236,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
     for (int c = 0; c < NOUT; c += 32) {
       float v[32], u[32];
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the stores
       tmem_ld32(trow + c, v);
       if (EPI == kEpiSwiGLU) tmem_ld32(trow + BN / 2 + c, u);
       const int n = n0 + c;

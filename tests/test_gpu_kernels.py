@@ -7,10 +7,13 @@ the tcgen05 GEMM (bf16, > 32 rows) and the SIMT kernel (fp32).
 Tolerances: the reference applies the same rounding points (round the
 product to bf16; round again after the residual add; round gate, up,
 silu(gate) and the product for SwiGLU) to an fp32 accumulation.  Two fp32
-accumulations in different orders differ by ~1e-6 relative, which can move a
-bf16 rounding by one unit in the last place, so the bar is 1 ulp for a plain
-product, 2 ulp after a residual add and 3 ulp through SwiGLU.  fp32: 1e-5
-relative to the output's largest magnitude.
+accumulations in different orders differ by a few fp32 units of the sum of
+|x_k * w_k|, which can move a bf16 rounding by one unit in the last place.
+The bar per element is therefore
+    1 ulp (plain product), 2 ulp (after the residual add), 3 ulp (SwiGLU)
+    + 3e-5 * sum_k |x_k * w_k|   (the accumulation-order term, which matters
+                                   only where the result nearly cancels).
+fp32: 1e-5 relative to the output's largest magnitude.
 """
 from __future__ import annotations
 
@@ -29,26 +32,35 @@ def bf16_ulp(t: torch.Tensor) -> torch.Tensor:
 
 
 def reference(x, w, epilogue, residual=None):
+    """(expected output, accumulation-order error term) in fp32."""
     torch.backends.cuda.matmul.allow_tf32 = False
     rt = (lambda v: v.to(x.dtype).float())
+    xa = x.float().abs()
     if epilogue == "swiglu":
         n = w.shape[0] // 2
         g = rt(x.float() @ w[:n].float().T)
         u = rt(x.float() @ w[n:].float().T)
-        return rt(rt(g / (1 + torch.exp(-g))) * u)
+        sg = rt(g / (1 + torch.exp(-g)))
+        dg = xa @ w[:n].float().abs().T
+        du = xa @ w[n:].float().abs().T
+        return rt(sg * u), 3e-5 * (dg * (u.abs() + 1) + du * (sg.abs() + 1))
     acc = x.float() @ w.float().T
+    slack = 3e-5 * (xa @ w.float().abs().T)
     if epilogue == "resid":
-        return rt(residual.float() + rt(acc))
-    return rt(acc)
+        # a one-ulp move of round(acc) survives the add even where R cancels it
+        return rt(residual.float() + rt(acc)), slack + bf16_ulp(rt(acc))
+    return rt(acc), slack
 
 
 def check(y, ref, dtype, ulps):
+    ref, slack = ref
     if dtype == torch.float32:
         assert (y.float() - ref).abs().max() <= 1e-5 * ref.abs().max()
         return
-    err = (y.float() - ref).abs() / bf16_ulp(ref)
-    bad = err > ulps
-    assert not bad.any(), f"{int(bad.sum())} elements beyond {ulps} ulp (max {float(err.max()):.2f})"
+    err = (y.float() - ref).abs()
+    bad = err > ulps * bf16_ulp(ref) + slack
+    worst = float((err / bf16_ulp(ref)).max())
+    assert not bad.any(), f"{int(bad.sum())} elements beyond the bar (worst {worst:.1f} ulp)"
 
 
 SHAPES = [
