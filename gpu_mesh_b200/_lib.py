@@ -189,3 +189,7 @@ SIGNATURES["mg_linear"] = (
     [_i32, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, ctypes.c_uint64, _vp],
 )
 SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i32])
+SIGNATURES["mg_linear_noalloc"] = (
+    ctypes.c_int,
+    [_i32, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp],
+)

@@ -17,6 +17,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -938,3 +939,51 @@ int mg_sample_top_p(const void* logits, int32_t dtype, int32_t rows, int32_t voc
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// mg_linear without allocation: the split-K scratch is a fixed array in the
+// library instead of caller- or stage-owned memory.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratch = MG_LINEAR_NOALLOC_SCRATCH;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratch];
+
+// Device address of this process's copy of the array, per device.  In host
+// code `g_noalloc_scratch` names a host-side stand-in, never the device
+// memory, so the address must come from cudaGetSymbolAddress.
+float* g_noalloc_ptr[64] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  MG_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(MG_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    MG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_ptr[dev] = (float*)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MG_OK;
+}
+
+}  // namespace
+
+extern "C" int mg_linear_noalloc(int32_t dtype, const void* X, int64_t ldx, const void* W,
+                                 int32_t M, int32_t N, int32_t K, int32_t epilogue, const void* R,
+                                 int64_t ldr, void* Y, int64_t ldy, void* stream) {
+  if (M < 0 || N < 1 || K < 1) return fail(MG_EINVAL, "invalid linear arguments");
+  const uint64_t need = linear_scratch_elems(dtype, M, N, K, epilogue);
+  if (need > kNoAllocScratch)
+    return fail(MG_EINVAL,
+                "this shape needs %llu fp32 elements of split-K scratch; mg_linear_noalloc holds "
+                "%llu (use mg_linear with caller scratch)",
+                (unsigned long long)need, (unsigned long long)kNoAllocScratch);
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return mg_linear(dtype, X, ldx, W, M, N, K, epilogue, R, ldr, Y, ldy, scratch, kNoAllocScratch,
+                   stream);
+}

@@ -218,6 +218,29 @@ int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t 
 /* fp32 scratch elements mg_linear needs for this shape. */
 uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32_t epilogue);
 
+/* The same linear layer as mg_linear, for callers that cannot allocate
+ * device memory: a process whose device memory is owned by another
+ * allocator (a serving framework's caching allocator, say) and may not take
+ * cudaMalloc / cudaFree behind it, or a latency-bound loop that cannot afford
+ * the device-wide synchronisation those calls bring.  No counterpart in the
+ * reference, which has no kernels of its own.
+ *
+ * It takes no scratch argument and allocates nothing: the split-K scratch of
+ * the decode GEMV is one fixed array in the library (MG_LINEAR_NOALLOC_SCRATCH
+ * fp32 elements, 4 MiB), present on every GPU that loads the library until
+ * the process exits.  That covers the decode layers of the benchmark models
+ * up to 16 token rows; a shape whose split-K needs more fails with MG_EINVAL
+ * and says how much it needs.  The first call on a device looks up
+ * that device's copy of the array, so make the first call (per device) before
+ * any stream capture.  All calls on one device within a process share the
+ * array and leave their partial sums in it (nothing in it needs to start at
+ * zero); two calls that overlap on the GPU, for example on two streams, race
+ * on it, so serialise them. */
+#define MG_LINEAR_NOALLOC_SCRATCH (1024u * 1024u)
+int mg_linear_noalloc(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t M,
+                      int32_t N, int32_t K, int32_t epilogue, const void* R, int64_t ldr, void* Y,
+                      int64_t ldy, void* stream);
+
 /* ---- Instrumentation (no counterpart in the reference, which has no
  * kernels of its own; used by the benchmark to report roofline fractions) ---- */
 
