@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "linear_tc.h"
 #include "meshgpu_b200.h"
 
 using namespace mg;
@@ -110,6 +111,8 @@ struct mg_stage {
   size_t work_bytes = 0;
   int work_tokens = 0, work_rows = 0;
   size_t work_scratch = 0;
+  int* counters = nullptr;  // stream-K tile counters: zero between launches
+  size_t counters_elems = 0;
   void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
   float* part = nullptr;
   RowDesc* rows = nullptr;
@@ -217,6 +220,12 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   const size_t o_h = take((size_t)Mt * st->I * e);
   const size_t o_part = take(std::max<size_t>(scr, 1) * sizeof(float));
   const size_t o_rows = take((size_t)Rt * sizeof(RowDesc));
+  size_t n_counters = 0;
+  n_counters = std::max(n_counters, gemv_tc_tiles(st->Nqkv, kEpiStore));
+  n_counters = std::max(n_counters, gemv_tc_tiles(st->H, kEpiResid));
+  n_counters = std::max(n_counters, gemv_tc_tiles(st->I, kEpiSwiGLU));
+  if (st->cfg.has_lm_head) n_counters = std::max(n_counters, gemv_tc_tiles(st->V, kEpiStore));
+  const size_t o_counters = take(n_counters * sizeof(int));
   if (st->work) {
     MG_CUDA(cudaDeviceSynchronize(), "synchronize before work resize");
     cudaFree(st->work);
@@ -239,6 +248,9 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   st->h = base + o_h;
   st->part = (float*)(base + o_part);
   st->rows = (RowDesc*)(base + o_rows);
+  st->counters = (int*)(base + o_counters);
+  st->counters_elems = n_counters;
+  MG_CUDA(cudaMemset(st->counters, 0, n_counters * sizeof(int)), "zero tile counters");
   st->work_bytes = off;
   st->work_tokens = Mt;
   st->work_rows = Rt;
@@ -404,6 +416,8 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   la.partial = st->part;
   la.partial_elems = st->work_scratch;
   la.err = st->err;
+  la.counters = st->counters;
+  la.counters_elems = st->counters_elems;
   la.M = M;
 
   QkvPostArgs qa{};
@@ -439,6 +453,7 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   aa.mask = c.attention_impl;
   aa.max_keys = max_keys;
   aa.scale = 1.0f / sqrtf((float)st->D);
+  aa.err = st->err;
 
   const int qd = st->nq * st->D;
   const double norm_bytes = 2.0 * M * H * st->esz;
@@ -862,6 +877,13 @@ int mg_stage_check_device(mg_stage* st, void* stream) {
   MG_CUDA(cudaMemset(st->err, 0, sizeof(int)), "error word reset");
   if (h == kErrTokenRange)
     return fail(MG_EDEVICE, "input_ids contain a value outside [0, %d)", st->cfg.vocab_size);
+  if (h == 3) {
+    // A tensor-core kernel gave up waiting for its data; its tile counters
+    // may be left mid-count, so clear them before the next forward.
+    if (st->counters) cudaMemset(st->counters, 0, st->counters_elems * sizeof(int));
+    return fail(MG_EDEVICE, "a tensor-core kernel timed out waiting for its data; the outputs of "
+                            "the forwards since the last check are invalid");
+  }
   return fail(MG_EDEVICE, "position_ids contain a value outside [0, %d)",
               st->cfg.max_position_embeddings);
 }

@@ -331,6 +331,7 @@ cudaError_t simt_dispatch(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue) {
+  if (gemv_tc_applicable(dtype, M, N, K)) return gemv_tc_scratch_elems(M, N, K, epilogue, true);
   if (gemv_applicable(dtype, M, N, K)) {
     const GemvPlan p = gemv_plan(M, N, K, epilogue);
     if (p.ksplit <= 1) return 0;
@@ -343,6 +344,7 @@ size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue) {
 
 cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s) {
   if (a.M == 0) return cudaSuccess;
+  if (gemv_tc_applicable(a.dtype, a.M, a.N, a.K)) return launch_gemv_tc(a, s);
   if (gemv_applicable(a.dtype, a.M, a.N, a.K)) {
     GemvPlan p = gemv_plan(a.M, a.N, a.K, a.epilogue);
     if (p.ksplit > 1 &&

@@ -52,6 +52,11 @@ struct LinearArgs {
   float* partial;               // split-K scratch, fp32
   size_t partial_elems;         // capacity of `partial`
   int* err;                     // stage error word (bounded-wait timeouts)
+  // Tile counters of the stream-K decode GEMM.  They must be zero when a
+  // launch starts and are zero again when it ends.  NULL: carved from the
+  // front of `partial` and cleared by the launcher before every launch.
+  int* counters;
+  size_t counters_elems;
 };
 
 // Scratch (fp32 elements) that launch_linear needs for the given shape.
@@ -92,6 +97,7 @@ struct AttnArgs {
   int B, S, nq, nkv, D, layer, mask;
   int max_keys;             // upper bound of keys any row can see (past + S)
   float scale;
+  int* err;                 // stage error word (bounded-wait timeouts)
 };
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);

@@ -9,4 +9,13 @@ bool linear_tc_applicable(int dtype, int M, int N, int K);
 size_t linear_tc_scratch_elems(int M, int N, int K, int epilogue);
 cudaError_t launch_linear_tc(const LinearArgs& a, cudaStream_t s);
 
+// Decode linear layers (<= 32 token rows): stream-K tcgen05 weight stream.
+bool gemv_tc_applicable(int dtype, int M, int N, int K);
+// fp32 scratch: partial-sum slots, plus the tile counters when the caller
+// does not provide a separate counter array.
+size_t gemv_tc_scratch_elems(int M, int N, int K, int epilogue, bool with_counters);
+// Tile counters a launch needs.
+size_t gemv_tc_tiles(int N, int epilogue);
+cudaError_t launch_gemv_tc(const LinearArgs& a, cudaStream_t s);
+
 }  // namespace mg

@@ -233,9 +233,10 @@ uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32
  * and says how much it needs.  The first call on a device looks up
  * that device's copy of the array, so make the first call (per device) before
  * any stream capture.  All calls on one device within a process share the
- * array and leave their partial sums in it (nothing in it needs to start at
- * zero); two calls that overlap on the GPU, for example on two streams, race
- * on it, so serialise them. */
+ * array and leave their partial sums in it; the tile counters at its front
+ * must start at zero, so every call clears them first (an asynchronous
+ * memset on `stream`, no allocation).  Two calls that overlap on the GPU,
+ * for example on two streams, race on the array, so serialise them. */
 #define MG_LINEAR_NOALLOC_SCRATCH (1024u * 1024u)
 int mg_linear_noalloc(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t M,
                       int32_t N, int32_t K, int32_t epilogue, const void* R, int64_t ldr, void* Y,

@@ -43,7 +43,9 @@ def reference(x, w, epilogue, residual=None):
         sg = rt(g / (1 + torch.exp(-g)))
         dg = xa @ w[:n].float().abs().T
         du = xa @ w[n:].float().abs().T
-        return rt(sg * u), 3e-5 * (dg * (u.abs() + 1) + du * (sg.abs() + 1))
+        # one-ulp moves of the rounded gate, up and silu(gate) carried to the product
+        flips = 1.1 * bf16_ulp(g) * u.abs() + bf16_ulp(u) * sg.abs() + bf16_ulp(sg) * u.abs()
+        return rt(sg * u), 3e-5 * (dg * (u.abs() + 1) + du * (sg.abs() + 1)) + flips
     acc = x.float() @ w.float().T
     slack = 3e-5 * (xa @ w.float().abs().T)
     if epilogue == "resid":
