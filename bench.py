@@ -23,7 +23,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -32,6 +31,8 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+
+from gpu_mesh_b200.clocks import ClockSampler  # noqa: E402
 
 METRIC = "decode tok/s (Llama-3-8B arch, 1/2/4/8 B200 stages); attn-decode HBM % of peak"
 FALLBACK_HBM_GBS = 6650.0
@@ -54,63 +55,6 @@ def peaks() -> tuple[float, float, str]:
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
-
-
-class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, gpu: int) -> None:
-        self.gpu = gpu
-        self.proc = None
-
-    def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
-            )
-        except (FileNotFoundError, OSError):
-            self.proc = None
-        return self
-
-    def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
-
-    def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        sm.sort()
-        return {
-            "sm_mhz": sm[len(sm) // 2] if sm else None,
-            "sm_max_mhz": mx,
-            "reasons": sorted(reasons),
-            "samples": len(sm),
-        }
 
 
 # ---------------------------------------------------------------------------
