@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "linear_tc.h"
+#include "tc_common.cuh"
 #include "meshgpu_b200.h"
 
 using namespace mg;
@@ -75,6 +76,7 @@ struct Slot {
   int batch = 0, cap = 0, len = 0;
   void* kv = nullptr;
   size_t bytes = 0;
+  void* tmap = nullptr;  // device copy of the KV tensor map (bf16, D 64/128), or NULL
 };
 
 struct ProfRec {
@@ -297,6 +299,19 @@ int reserve_slot(mg_stage* st, int id, int batch, int need, cudaStream_t s) {
   sl.cap = cap;
   sl.bytes = bytes;
   st->kv_bytes += bytes;
+  // Tensor map of the block for the tensor-core attention: a 2-D bf16 view
+  // [layers*2*rows*nkv*cap, D], box kKvBoxKeys keys x 64 dims.
+  if (attention_tc_applicable(st->cfg.dtype, st->D, st->nq / st->nkv)) {
+    CUtensorMap tm;
+    const uint64_t rows = (uint64_t)st->L * 2 * sl.batch * st->nkv * cap;
+    if (rows < (1ull << 31) && tc_host::make_map(&tm, kv, rows, st->D, st->D, kKvBoxKeys)) {
+      if (!sl.tmap) MG_CUDA(cudaMalloc(&sl.tmap, sizeof(CUtensorMap)), "KV tensor map");
+      MG_CUDA(cudaMemcpy(sl.tmap, &tm, sizeof(CUtensorMap), cudaMemcpyHostToDevice), "KV tensor map upload");
+    } else if (sl.tmap) {
+      cudaFree(sl.tmap);
+      sl.tmap = nullptr;
+    }
+  }
   return MG_OK;
 }
 
@@ -308,6 +323,7 @@ void drop_slot(mg_stage* st, int id) {
     cudaFree(it->second.kv);
     st->kv_bytes -= it->second.bytes;
   }
+  if (it->second.tmap) cudaFree(it->second.tmap);
   st->slots.erase(it);
 }
 
@@ -454,6 +470,8 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   aa.max_keys = max_keys;
   aa.scale = 1.0f / sqrtf((float)st->D);
   aa.err = st->err;
+  aa.use_tc = 1;
+  for (const RowDesc& r : rows) aa.use_tc &= r.kv_tmap != 0;
 
   const int qd = st->nq * st->D;
   const double norm_bytes = 2.0 * M * H * st->esz;
@@ -679,8 +697,10 @@ int mg_stage_destroy(mg_stage* st) {
   if (!st) return MG_OK;
   DeviceGuard guard(st->cfg.device);
   cudaDeviceSynchronize();
-  for (auto& kv : st->slots)
+  for (auto& kv : st->slots) {
     if (kv.second.kv) cudaFree(kv.second.kv);
+    if (kv.second.tmap) cudaFree(kv.second.tmap);
+  }
   if (st->work) cudaFree(st->work);
   if (st->wbuf) cudaFree(st->wbuf);
   if (st->err) cudaFree(st->err);
@@ -824,7 +844,7 @@ int mg_stage_forward(mg_stage* st, int32_t slot, const int64_t* ids, const void*
   Slot& sl = st->slots[slot];
   std::vector<RowDesc> rows(batch);
   for (int b = 0; b < batch; ++b)
-    rows[b] = RowDesc{(uint64_t)sl.kv, sl.batch, b, sl.cap, past};
+    rows[b] = RowDesc{(uint64_t)sl.kv, (uint64_t)sl.tmap, sl.batch, b, sl.cap, past};
   rc = run_stage(st, rows, seq, ids, hidden_in, positions, out_mode, out, s);
   if (rc) return rc;
   sl.len = past + seq;
@@ -858,7 +878,7 @@ int mg_stage_decode_multi(mg_stage* st, const int32_t* slots, int32_t n_slots, c
   for (int i = 0; i < n_slots; ++i) {
     const Slot& sl = st->slots[slots[i]];
     for (int b = 0; b < sl.batch; ++b)
-      rows.push_back(RowDesc{(uint64_t)sl.kv, sl.batch, b, sl.cap, sl.len});
+      rows.push_back(RowDesc{(uint64_t)sl.kv, (uint64_t)sl.tmap, sl.batch, b, sl.cap, sl.len});
   }
   rc = run_stage(st, rows, 1, ids, hidden_in, nullptr, out_mode, out, s);
   if (rc) return rc;

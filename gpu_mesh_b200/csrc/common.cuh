@@ -92,4 +92,14 @@ __device__ __forceinline__ void flag_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Programmatic dependent launch.  Every kernel of the stage is launched with
+// programmatic stream serialisation, so it may start while the kernel before
+// it in the stream is still running.  pdl_wait() blocks until that kernel has
+// completed and its writes are visible: call it before reading anything the
+// previous kernel produced and before writing anything it might still read.
+// pdl_trigger() lets the next kernel launch early; its own pdl_wait() keeps it
+// correct.  Both are no-ops when there is no programmatic dependency.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace mg

@@ -64,6 +64,8 @@ struct AttnLayout {
 
 template <typename T, int LPK, int GM>
 __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   using L = AttnLayout<T, LPK, GM>;
   constexpr int VEC = L::VEC, D = L::D, KPW = 32 / LPK, NW = kAttnWarps;
   extern __shared__ uint8_t smem_raw[];
@@ -196,6 +198,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(AttnArgs a) {
 
 template <typename T>
 __global__ void attn_combine_kernel(AttnArgs a, int splits) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, hq = blockIdx.y;
   const int G = a.nq / a.nkv, D = a.D;
   const int h = hq / G, g = hq % G;
@@ -233,8 +237,7 @@ cudaError_t attn_launch_one(const AttnArgs& a, dim3 grid, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  attn_chunk_kernel<T, LPK, GM><<<grid, kAttnThreads, smem, s>>>(a);
-  note_launch();
+  { const cudaError_t _le = launch_pdl(attn_chunk_kernel<T, LPK, GM>, dim3(grid), dim3(kAttnThreads), smem, s, a); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 
@@ -280,16 +283,18 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   if (attention_scratch_elems(M, a.nq, a.D, a.max_keys) > a.partial_elems)
     return cudaErrorInvalidValue;
   dim3 grid(M, a.nkv, splits);
-  cudaError_t e = (a.dtype == kBF16) ? attn_launch<__nv_bfloat16>(a, grid, s)
-                                     : attn_launch<float>(a, grid, s);
+  cudaError_t e;
+  if (a.use_tc && attention_tc_applicable(a.dtype, a.D, a.nq / a.nkv))
+    e = launch_attention_tc(a, grid, s);  // same 128-key chunks and partial format
+  else
+    e = (a.dtype == kBF16) ? attn_launch<__nv_bfloat16>(a, grid, s) : attn_launch<float>(a, grid, s);
   if (e != cudaSuccess) return e;
   dim3 cgrid(M, a.nq);
   const int threads = a.D < 128 ? a.D : 128;
   if (a.dtype == kBF16)
-    attn_combine_kernel<__nv_bfloat16><<<cgrid, threads, 0, s>>>(a, splits);
+    { const cudaError_t _le = launch_pdl(attn_combine_kernel<__nv_bfloat16>, dim3(cgrid), dim3(threads), 0, s, a, splits); if (_le != cudaSuccess) return _le; }
   else
-    attn_combine_kernel<float><<<cgrid, threads, 0, s>>>(a, splits);
-  note_launch();
+    { const cudaError_t _le = launch_pdl(attn_combine_kernel<float>, dim3(cgrid), dim3(threads), 0, s, a, splits); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -12,6 +12,8 @@ namespace {
 template <typename T>
 __global__ void embed_kernel(const T* __restrict__ table, const int64_t* __restrict__ ids, int H,
                              int V, T* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x;
   int64_t id = ids[m];
   if (id < 0 || id >= V) {
@@ -40,6 +42,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __restrict__ w, int H,
                                float eps, T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int m = blockIdx.x;
   const T* xr = x + (size_t)m * xs;
@@ -66,6 +70,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __r
 template <typename T>
 __global__ void kv_copy_kernel(T* __restrict__ kv, int layer, int kvsel, int slot_rows, int nkv,
                                int cap, int D, int len, T* __restrict__ ext, bool to_slot) {
+  pdl_trigger();
+  pdl_wait();
   // grid: (len, nkv, slot_rows); block covers D.
   const int pos = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
   T* sp = kv + kv_offset_elems(layer, kvsel, slot_rows, r, nkv, h, cap, D, pos);
@@ -82,10 +88,10 @@ cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M
                          void* out, int* err, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (dtype == kBF16)
-    { embed_kernel<__nv_bfloat16><<<M, 128, 0, s>>>((const __nv_bfloat16*)table, ids, H, V,
-                                                  (__nv_bfloat16*)out, err); note_launch(); }
+    { const cudaError_t _le = launch_pdl(embed_kernel<__nv_bfloat16>, dim3(M), dim3(128), 0, s, (const __nv_bfloat16*)table, ids, H, V,
+                                                  (__nv_bfloat16*)out, err); if (_le != cudaSuccess) return _le; }
   else
-    { embed_kernel<float><<<M, 128, 0, s>>>((const float*)table, ids, H, V, (float*)out, err); note_launch(); }
+    { const cudaError_t _le = launch_pdl(embed_kernel<float>, dim3(M), dim3(128), 0, s, (const float*)table, ids, H, V, (float*)out, err); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 
@@ -94,11 +100,11 @@ cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t xs, const void* w, 
   if (M == 0) return cudaSuccess;
   const int threads = H >= 2048 ? 256 : 128;
   if (dtype == kBF16)
-    { rmsnorm_kernel<__nv_bfloat16><<<M, threads, 0, s>>>(
-        (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y); note_launch(); }
+    { const cudaError_t _le = launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(threads), 0, s, 
+        (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y); if (_le != cudaSuccess) return _le; }
   else
-    { rmsnorm_kernel<float><<<M, threads, 0, s>>>((const float*)x, xs, (const float*)w, H, eps,
-                                                (float*)y); note_launch(); }
+    { const cudaError_t _le = launch_pdl(rmsnorm_kernel<float>, dim3(M), dim3(threads), 0, s, (const float*)x, xs, (const float*)w, H, eps,
+                                                (float*)y); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 
@@ -108,12 +114,12 @@ cudaError_t launch_kv_copy(int dtype, void* kv_base, int layer, int kv, int slot
   dim3 grid(len, nkv, slot_rows);
   const int threads = D < 128 ? D : 128;
   if (dtype == kBF16)
-    { kv_copy_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>((__nv_bfloat16*)kv_base, layer, kv,
+    { const cudaError_t _le = launch_pdl(kv_copy_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, s, (__nv_bfloat16*)kv_base, layer, kv,
                                                            slot_rows, nkv, cap, D, len,
-                                                           (__nv_bfloat16*)ext, to_slot); note_launch(); }
+                                                           (__nv_bfloat16*)ext, to_slot); if (_le != cudaSuccess) return _le; }
   else
-    { kv_copy_kernel<float><<<grid, threads, 0, s>>>((float*)kv_base, layer, kv, slot_rows, nkv, cap,
-                                                   D, len, (float*)ext, to_slot); note_launch(); }
+    { const cudaError_t _le = launch_pdl(kv_copy_kernel<float>, dim3(grid), dim3(threads), 0, s, (float*)kv_base, layer, kv, slot_rows, nkv, cap,
+                                                   D, len, (float*)ext, to_slot); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -156,18 +156,13 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   const uint32_t tmem = *tmem_holder;
   long long issued = 0;
 
+  pdl_trigger();
   if (warp == 0) {
     if (lane == 0) {
-      // TMA producer over this CTA's units.
-      for (long long u = u0; u < u1; ++u) {
-        const long long i = u - u0;
-        const int s = (int)(i % kStagesD);
-        const int round = (int)(i / kStagesD);
-        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, err)) {
-          *abort_flag = 1;
-          break;
-        }
-        if (*abort_flag) break;
+      // TMA producer over this CTA's units.  The weights do not depend on the
+      // kernel before this one, so the first ring's worth of W is requested
+      // before waiting for it; the activations X only after.
+      auto load_w = [&](long long u, int s) {
         const int t = (int)(u / p.nk), kb = (int)(u % p.nk);
         const int r0 = (EPI == kEpiSwiGLU) ? t * 64 : t * kRows;
         const int r1 = (EPI == kEpiSwiGLU) ? a.N + t * 64 : t * kRows + 64;
@@ -175,7 +170,26 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         mbar_expect_tx(&full[s], L::kStage);
         tma_load_2d(st, &tm_w, &full[s], kb * kKB, r0);
         tma_load_2d(st + kWBytes / 2, &tm_w, &full[s], kb * kKB, r1);
-        tma_load_2d(st + kWBytes, &tm_x, &full[s], kb * kKB, 0);
+      };
+      auto load_x = [&](long long u, int s) {
+        tma_load_2d(smem + s * L::kStage + kWBytes, &tm_x, &full[s], (int)(u % p.nk) * kKB, 0);
+      };
+      const long long pre = min((long long)kStagesD, u1 - u0);
+      for (long long i = 0; i < pre; ++i) load_w(u0 + i, (int)i);
+      pdl_wait();
+      for (long long i = 0; i < pre; ++i) load_x(u0 + i, (int)i);
+      issued = pre;
+      for (long long u = u0 + pre; u < u1; ++u) {
+        const long long i = u - u0;
+        const int s = (int)(i % kStagesD);
+        const int round = (int)(i / kStagesD);
+        if (!mbar_wait(&empty[s], (round - 1) & 1, err)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        load_w(u, s);
+        load_x(u, s);
         issued = i + 1;
       }
     }
@@ -213,7 +227,8 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       mma_commit(drain);
     }
   } else {
-    // Epilogue warps 2-5.
+    // Epilogue warps 2-5: they read R and write Y, slots and counters.
+    pdl_wait();
     const int q = warp & 3;
     const int r = q * 32 + lane;  // W row within the tile
     int pi = 0;
@@ -244,15 +259,29 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         __threadfence();
 #pragma unroll
         for (int i = 0; i < NP; ++i) v[i] = 0.f;
-        for (int cc = c_lo; cc <= c_hi; ++cc) {
-          const float4* S = reinterpret_cast<const float4*>(slots + ((size_t)p.slot(cc, t) * kRows + r) * NP);
+        // Pieces are added in CTA order (deterministic); their loads are issued
+        // kBatch pieces at a time so the L2 round trips overlap.
+        constexpr int kBatch = NP == 16 ? 4 : 2;
+        for (int c0 = c_lo; c0 <= c_hi; c0 += kBatch) {
+          float4 buf[kBatch][NP / 4];
 #pragma unroll
-          for (int i = 0; i < NP / 4; ++i) {
-            const float4 x = __ldcg(S + i);
-            v[4 * i] += x.x;
-            v[4 * i + 1] += x.y;
-            v[4 * i + 2] += x.z;
-            v[4 * i + 3] += x.w;
+          for (int b2 = 0; b2 < kBatch; ++b2) {
+            if (c0 + b2 > c_hi) break;
+            const float4* S =
+                reinterpret_cast<const float4*>(slots + ((size_t)p.slot(c0 + b2, t) * kRows + r) * NP);
+#pragma unroll
+            for (int i = 0; i < NP / 4; ++i) buf[b2][i] = __ldcg(S + i);
+          }
+#pragma unroll
+          for (int b2 = 0; b2 < kBatch; ++b2) {
+            if (c0 + b2 > c_hi) break;
+#pragma unroll
+            for (int i = 0; i < NP / 4; ++i) {
+              v[4 * i] += buf[b2][i].x;
+              v[4 * i + 1] += buf[b2][i].y;
+              v[4 * i + 2] += buf[b2][i].z;
+              v[4 * i + 3] += buf[b2][i].w;
+            }
           }
         }
         if (threadIdx.x == 64) counters[t] = 0;
@@ -334,7 +363,7 @@ cudaError_t launch(const LinearArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  { gemv_tc_kernel<NP, EPI><<<p.G, kThreadsD, smem, s>>>(tw, tx, a, p, counters, slots, a.err); note_launch(); }
+  { const cudaError_t _le = launch_pdl(gemv_tc_kernel<NP, EPI>, dim3(p.G), dim3(kThreadsD), smem, s, tw, tx, a, p, counters, slots, a.err); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -47,6 +47,8 @@ __device__ __forceinline__ void epi_write(const LinearArgs& a, int tok, int n, f
 // ---------------------------------------------------------------------------
 template <typename T, int EPI>
 __global__ void __launch_bounds__(256) linear_simt_kernel(LinearArgs a) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int BM = 64, BN = 64, BK = 16;
   constexpr int NB = (EPI == kEpiSwiGLU) ? 2 : 1;
   __shared__ float Xs[BK][BM + 4];
@@ -137,6 +139,8 @@ constexpr int kGemvChunk = 32 * kGemvU;
 // matching up rows N + [32*tile, +32).
 template <int MT, int EPI>
 __global__ void __launch_bounds__(kGemvNW * 32) gemv_mma_kernel(LinearArgs a, int chunks_per_split) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int RG = kGemvRG, U = kGemvU, NW = kGemvNW;
   const bf16* __restrict__ X = (const bf16*)a.X;
   const bf16* __restrict__ W = (const bf16*)a.W;
@@ -255,6 +259,8 @@ __global__ void __launch_bounds__(kGemvNW * 32) gemv_mma_kernel(LinearArgs a, in
 
 template <typename T, int EPI>
 __global__ void splitk_reduce_kernel(LinearArgs a, int ksplit) {
+  pdl_trigger();
+  pdl_wait();
   const int ncols = (EPI == kEpiSwiGLU) ? 2 * a.N : a.N;
   const size_t total = (size_t)a.M * a.N;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
@@ -295,11 +301,11 @@ GemvPlan gemv_plan(int M, int N, int K, int epi) {
 template <int MT, int EPI>
 cudaError_t gemv_launch(const LinearArgs& a, const GemvPlan& p, cudaStream_t s) {
   dim3 grid(p.tiles, p.ksplit);
-  { gemv_mma_kernel<MT, EPI><<<grid, kGemvNW * 32, 0, s>>>(a, p.cps); note_launch(); }
+  { const cudaError_t _le = launch_pdl(gemv_mma_kernel<MT, EPI>, dim3(grid), dim3(kGemvNW * 32), 0, s, a, p.cps); if (_le != cudaSuccess) return _le; }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.ksplit == 1) return e;
   const int blocks = (int)std::min<size_t>(((size_t)a.M * a.N + 255) / 256, 148 * 8);
-  { splitk_reduce_kernel<bf16, EPI><<<blocks, 256, 0, s>>>(a, p.ksplit); note_launch(); }
+  { const cudaError_t _le = launch_pdl(splitk_reduce_kernel<bf16, EPI>, dim3(blocks), dim3(256), 0, s, a, p.ksplit); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 
@@ -315,7 +321,7 @@ cudaError_t gemv_dispatch(const LinearArgs& a, const GemvPlan& p, cudaStream_t s
 template <typename T, int EPI>
 cudaError_t simt_launch(const LinearArgs& a, cudaStream_t s) {
   dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
-  { linear_simt_kernel<T, EPI><<<grid, 256, 0, s>>>(a); note_launch(); }
+  { const cudaError_t _le = launch_pdl(linear_simt_kernel<T, EPI>, dim3(grid), dim3(256), 0, s, a); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -80,6 +80,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_holder;
 
+  // Barrier and TMEM set-up above overlap the previous kernel's tail.
+  pdl_trigger();
+  pdl_wait();
   int issued = 0;
   if (warp == 0 && lane == 0) {
     // TMA producer.
@@ -198,7 +201,7 @@ cudaError_t launch_tc(const LinearArgs& a, cudaStream_t s) {
   }
   const int ntile = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
   dim3 grid((a.N + ntile - 1) / ntile, (a.M + kBM - 1) / kBM);
-  { gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, s>>>(tx, tw, a, a.err); note_launch(); }
+  { const cudaError_t _le = launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kThreads), smem, s, tx, tw, a, a.err); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

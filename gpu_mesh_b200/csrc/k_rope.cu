@@ -17,6 +17,8 @@ constexpr int kHeadsPerCta = 4;
 
 template <typename T>
 __global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_kernel(QkvPostArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float xs[kHeadsPerCta][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m = blockIdx.x;
@@ -83,9 +85,9 @@ cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   dim3 grid(M, (a.nq + 2 * a.nkv + kHeadsPerCta - 1) / kHeadsPerCta);
   if (a.dtype == kBF16)
-    { qkv_post_kernel<__nv_bfloat16><<<grid, kHeadsPerCta * 32, 0, s>>>(a); note_launch(); }
+    { const cudaError_t _le = launch_pdl(qkv_post_kernel<__nv_bfloat16>, dim3(grid), dim3(kHeadsPerCta * 32), 0, s, a); if (_le != cudaSuccess) return _le; }
   else
-    { qkv_post_kernel<float><<<grid, kHeadsPerCta * 32, 0, s>>>(a); note_launch(); }
+    { const cudaError_t _le = launch_pdl(qkv_post_kernel<float>, dim3(grid), dim3(kHeadsPerCta * 32), 0, s, a); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -42,6 +42,8 @@ template <typename T>
 __global__ void __launch_bounds__(kSampleThreads) argmax_kernel(const T* __restrict__ logits,
                                                                 int vocab, int64_t stride,
                                                                 int64_t* __restrict__ ids) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const T* row = logits + (size_t)blockIdx.x * stride;
@@ -117,6 +119,8 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
                                                                float temperature, float top_p,
                                                                const float* __restrict__ uniforms,
                                                                int64_t* __restrict__ ids) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   __shared__ int cnt_s[32];
   const T* row = logits + (size_t)blockIdx.x * stride;
@@ -218,10 +222,10 @@ cudaError_t launch_argmax(int dtype, const void* logits, int rows, int vocab, in
                           int64_t* ids, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   if (dtype == kBF16)
-    { argmax_kernel<__nv_bfloat16><<<rows, kSampleThreads, 0, s>>>((const __nv_bfloat16*)logits,
-                                                                 vocab, stride, ids); note_launch(); }
+    { const cudaError_t _le = launch_pdl(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(kSampleThreads), 0, s, (const __nv_bfloat16*)logits,
+                                                                 vocab, stride, ids); if (_le != cudaSuccess) return _le; }
   else
-    { argmax_kernel<float><<<rows, kSampleThreads, 0, s>>>((const float*)logits, vocab, stride, ids); note_launch(); }
+    { const cudaError_t _le = launch_pdl(argmax_kernel<float>, dim3(rows), dim3(kSampleThreads), 0, s, (const float*)logits, vocab, stride, ids); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 
@@ -231,11 +235,11 @@ cudaError_t launch_top_p(int dtype, const void* logits, int rows, int vocab, int
   if (rows == 0) return cudaSuccess;
   if (!(temperature > 0.f)) return launch_argmax(dtype, logits, rows, vocab, stride, ids, s);
   if (dtype == kBF16)
-    { top_p_kernel<__nv_bfloat16><<<rows, kSampleThreads, 0, s>>>(
-        (const __nv_bfloat16*)logits, vocab, stride, temperature, top_p, uniforms, ids); note_launch(); }
+    { const cudaError_t _le = launch_pdl(top_p_kernel<__nv_bfloat16>, dim3(rows), dim3(kSampleThreads), 0, s, 
+        (const __nv_bfloat16*)logits, vocab, stride, temperature, top_p, uniforms, ids); if (_le != cudaSuccess) return _le; }
   else
-    { top_p_kernel<float><<<rows, kSampleThreads, 0, s>>>((const float*)logits, vocab, stride,
-                                                        temperature, top_p, uniforms, ids); note_launch(); }
+    { const cudaError_t _le = launch_pdl(top_p_kernel<float>, dim3(rows), dim3(kSampleThreads), 0, s, (const float*)logits, vocab, stride,
+                                                        temperature, top_p, uniforms, ids); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

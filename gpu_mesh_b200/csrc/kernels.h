@@ -10,16 +10,46 @@ namespace mg {
 // Count `n` kernel launches (process-wide, read by mg_launch_count).
 void note_launch(int n = 1);
 
+// Launch `kernel` with programmatic stream serialisation (see pdl_wait /
+// pdl_trigger in common.cuh) and count it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  note_launch();
+  return e;
+}
+
 // One sequence row of a forward batch: where its KV cache lives and how long
 // it was before this forward.  Kept in device memory so that a captured decode
 // step reads the current lengths instead of baking them in.
 struct RowDesc {
   uint64_t kv_base;   // device address of the slot's KV block
+  uint64_t kv_tmap;   // device address of the slot's KV tensor map (bf16 D 64/128), or 0
   int32_t slot_rows;  // rows (batch) of the slot
   int32_t row;        // this row's index inside the slot
   int32_t cap;        // positions the slot can hold
   int32_t past;       // cached positions before this forward
 };
+
+// The KV tensor map of a slot views its block as a 2-D bf16 array
+// [layers*2*rows*nkv*cap, D] with a box of kKvBoxKeys keys x 64 dims and a
+// 128-byte swizzle; kv_row() is the row of (layer, K|V, row, head, pos).
+constexpr int kKvBoxKeys = 32;
+__host__ __device__ inline int64_t kv_row(int layer, int kv, int slot_rows, int row, int nkv,
+                                          int head, int cap, int pos) {
+  return ((((int64_t)(layer * 2 + kv) * slot_rows + row) * nkv + head) * cap + pos);
+}
 
 // KV block layout of a slot: [local_layer][2 (K,V)][slot_rows][nkv][cap][D].
 __host__ __device__ inline size_t kv_offset_elems(int layer, int kv, int slot_rows, int row,
@@ -98,9 +128,14 @@ struct AttnArgs {
   int max_keys;             // upper bound of keys any row can see (past + S)
   float scale;
   int* err;                 // stage error word (bounded-wait timeouts)
+  int use_tc;               // every row has a KV tensor map: tensor-core kernel
 };
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// Tensor-core attention (k_attention_tc.cu): bf16, head_dim 64 or 128, G <= 8.
+bool attention_tc_applicable(int dtype, int D, int G);
+cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s);
 
 cudaError_t launch_argmax(int dtype, const void* logits, int rows, int vocab, int64_t row_stride,
                           int64_t* ids, cudaStream_t s);

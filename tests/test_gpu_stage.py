@@ -272,3 +272,34 @@ def test_full_width_layers_match_oracle(cfg):
             ex = exact[0].forward(input_ids=nxt, key="f").float()
         _exact_bar(got.float().cpu(), ref, ex, f"decode {step}")
     w.close()
+
+
+@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 8), (64, 32, 4)], ids=["d128-g4", "d64-g8"])
+@pytest.mark.parametrize("T", [1, 31, 129, 1000, 4100])
+def test_attention_over_imported_cache_matches_oracle(D, nq, nkv, T):
+    """Decode attention (tensor-core path for bf16 head_dim 64/128) over a
+    cache pre-filled with N(0, 1) keys and values, at lengths that are not
+    multiples of the 32-key boxes or 128-key chunks."""
+    cfg = LlamaConfig(vocab_size=256, hidden_size=512, intermediate_size=1024, num_hidden_layers=1,
+                      num_attention_heads=nq, num_key_value_heads=nkv, head_dim=D,
+                      max_position_embeddings=8192, rope_theta=500000.0)
+    full = synthetic_model_state(cfg, seed=7, dtype=torch.bfloat16)
+    state = {k: v for k, v in full.items() if not k.startswith(("norm", "lm_head"))}
+    stage = B200Stage(cfg, 0, 1, has_embedding=True, has_lm_head=False, device=DEV,
+                      dtype=torch.bfloat16, state_dict=state)
+    oracle = R.OracleStage(cfg, 0, 1, True, False, state, torch.bfloat16)
+    exact = R.OracleStage(cfg, 0, 1, True, False, state, torch.bfloat16)
+    g = torch.Generator().manual_seed(T + D)
+    k = torch.randn(2, nkv, T, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(2, nkv, T, D, generator=g).to(torch.bfloat16)
+    stage.kv_reserve(3, 2, T + 8)
+    stage.kv_import(3, 0, k, v)
+    oracle.caches["c"] = [(k, v)]
+    exact.caches["c"] = [(k, v)]
+    ids = torch.tensor([[5], [77]])
+    got = stage.forward_slot(3, None, input_ids=ids).float().cpu()
+    ref = oracle.forward(input_ids=ids, key="c").float()
+    with R.exact_rounding():
+        ex = exact.forward(input_ids=ids, key="c").float()
+    _exact_bar(got, ref, ex, f"T={T}")
+    stage.close()
