@@ -12,7 +12,7 @@
 // mbarrier and values on another, so scoring overlaps the value load.
 //   S = Q·Kᵀ   A = Q (heads x dims, registers), B = K rows via ldmatrix
 //   P = exp(S·scale - max)   per head row, quad shuffles
-//   O = P·V    A = P (bf16, from S's accumulators), B = V via ldmatrix.trans
+//   O = P·V    A = P (bf16 hi + lo, from S's accumulators), B = V via ldmatrix.trans
 // The four warps' (max, sum, O) are merged in shared memory into the chunk's
 // partial, which the combine kernel (k_attention.cu) merges across chunks.
 // Every wait is bounded (code 3 in the error word on expiry).
@@ -74,6 +74,10 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
   return a | (b << 16);
 }
+
+// The two bf16 halves of a packed pair, widened.
+__device__ __forceinline__ float lo_bf16(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hi_bf16(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
 // Byte offset of (key row r, 16-byte chunk c of 64 dims) inside a swizzled box.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -219,8 +223,12 @@ __global__ void __launch_bounds__(kWarps * 32) attn_tc_kernel(AttnArgs a) {
     const uint32_t vbase = smem_u32(Vw);
 #pragma unroll
     for (int kt = 0; kt < 2; ++kt) {
+      // P = hi + lo, both bf16: two MMAs keep P to ~2^-17 relative, so the
+      // product matches an fp32 P·V instead of a bf16-rounded one.
       const uint32_t pa0 = pack2(sc[2 * kt][0], sc[2 * kt][1]);
       const uint32_t pa2 = pack2(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+      const uint32_t pl0 = pack2(sc[2 * kt][0] - lo_bf16(pa0), sc[2 * kt][1] - hi_bf16(pa0));
+      const uint32_t pl2 = pack2(sc[2 * kt + 1][0] - lo_bf16(pa2), sc[2 * kt + 1][1] - hi_bf16(pa2));
 #pragma unroll
       for (int dn = 0; dn < DN; dn += 2) {
         // matrices: keys 16kt+0..7 / +8..15, dim chunks dn / dn+1
@@ -231,7 +239,9 @@ __global__ void __launch_bounds__(kWarps * 32) attn_tc_kernel(AttnArgs a) {
         ldsm_x4_t(vbase + (c >> 3) * kBox + swz(r, c & 7), bfr);
         if (ok_v) {
           mma16816(o[dn], pa0, pa2, bfr[0], bfr[1]);
+          mma16816(o[dn], pl0, pl2, bfr[0], bfr[1]);
           mma16816(o[dn + 1], pa0, pa2, bfr[2], bfr[3]);
+          mma16816(o[dn + 1], pl0, pl2, bfr[2], bfr[3]);
         }
       }
     }

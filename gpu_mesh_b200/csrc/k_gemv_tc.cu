@@ -21,7 +21,9 @@
 // issues tcgen05.mma (M=128, N=NP, K=16) into one of two TMEM accumulators;
 // warps 2-5 drain the other accumulator with tcgen05.ld (warp w reads TMEM
 // lanes 32*(w%4)..+31) and run the epilogue (store / residual / SwiGLU with
-// the reference's rounding points).  Every wait is bounded; on a timeout the
+// the reference's rounding points).  Launched with programmatic dependent
+// launch, the producer requests its first weights before waiting for the
+// previous kernel.  Every wait is bounded; on a timeout the
 // kernel records code 3 in the error word, drains what it issued, frees its
 // TMEM and returns.
 #include "linear_tc.h"
@@ -35,7 +37,7 @@ using bf16 = __nv_bfloat16;
 
 constexpr int kRows = 128;
 constexpr int kKB = 64;
-constexpr int kStagesD = 8;
+constexpr int kStagesD = 8;  // 144-160 KB of weights in flight per SM
 constexpr int kThreadsD = 192;
 constexpr int kWBytes = kRows * kKB * 2;
 
@@ -86,7 +88,9 @@ __device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const f
       const int f = t * 64 + r;
       if (f < a.N) {
         bf16* Y = (bf16*)a.Y + f;
-        for (int tok = 0; tok < a.M; ++tok) {
+#pragma unroll
+        for (int tok = 0; tok < NP; ++tok) {
+          if (tok >= a.M) break;
           const float g = rt<bf16>(v[tok]), u = rt<bf16>(xchg[r * NP + tok]);
           const float sg = rt<bf16>(g / (1.0f + expf(-g)));
           Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(sg * u);
@@ -100,13 +104,20 @@ __device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const f
   if (f >= a.N) return;
   bf16* Y = (bf16*)a.Y + f;
   if (EPI == kEpiResid) {
+    // R may alias Y, so the compiler cannot hoist a load above the previous
+    // token's store: read every residual first, then write.
     const bf16* R = (const bf16*)a.R + f;
-    for (int tok = 0; tok < a.M; ++tok) {
-      const float rr = __bfloat162float(R[(size_t)tok * a.ldr]);
-      Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(rr + rt<bf16>(v[tok]));
-    }
+    float rr[NP];
+#pragma unroll
+    for (int tok = 0; tok < NP; ++tok)
+      rr[tok] = tok < a.M ? __bfloat162float(R[(size_t)tok * a.ldr]) : 0.f;
+#pragma unroll
+    for (int tok = 0; tok < NP; ++tok)
+      if (tok < a.M) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(rr[tok] + rt<bf16>(v[tok]));
   } else {
-    for (int tok = 0; tok < a.M; ++tok) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(v[tok]);
+#pragma unroll
+    for (int tok = 0; tok < NP; ++tok)
+      if (tok < a.M) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(v[tok]);
   }
 }
 
