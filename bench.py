@@ -38,12 +38,26 @@ METRIC = "decode tok/s (Llama-3-8B arch, 1/2/4/8 B200 stages); attn-decode HBM %
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one
+# `ncu --set full` capture of the same kernels on the 2-layer case of this
+# workload (identical per-layer shapes), next to the algorithmic bytes of the
+# same launches.  gemv_tc: o_proj, gate/up, down of layer 0 in the first decode
+# step (mean of the three); attn_tc: layers 0 and 1 of that step.
+NCU_TRAFFIC = {
+    "gemv_tc": {"dram_bytes": (34.13e6 + 245.32e6 + 124.31e6) / 3,
+                "algorithmic_bytes": (34.34e6 + 236.06e6 + 118.88e6) / 3,
+                "launches": "o_proj, gate/up, down of one layer at 32 rows"},
+    "attn_tc": {"dram_bytes": (144.31e6 + 144.61e6) / 2,
+                "algorithmic_bytes": 139.4e6,
+                "launches": "decode attention of one layer, 32 rows x 8 KV heads x 1025 keys"},
+}
 
-def llama3_8b():
+
+def llama3_8b(layers: int = 32):
     from gpu_mesh_b200.config import LlamaConfig
 
     return LlamaConfig(
-        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=layers,
         num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192,
         rms_norm_eps=1e-5, rope_theta=500000.0,
     )
@@ -115,7 +129,7 @@ def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cfg = llama3_8b()
+    cfg = llama3_8b(args.layers)
     base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=max(1, min(args.steps, 2)))
     steps = args.steps
     line = {
@@ -140,9 +154,12 @@ def run_reference_arm(args) -> None:
 
 
 def workload_config(args) -> dict:
+    layers = "" if args.layers == 32 else f" cut to {args.layers} layers (profiling case)"
     return {
-        "workload": "Llama-3-8B-architecture bf16 greedy decode, batch 32 as 4 micro-batches of 8, "
-                    f"{args.prompt}-token prompts",
+        "workload": f"Llama-3-8B-architecture{layers} bf16 greedy decode, batch "
+                    f"{args.micro * args.micro_batches} as {args.micro_batches} micro-batches of "
+                    f"{args.micro}, {args.prompt}-token prompts",
+        "layers": args.layers,
         "batch": args.micro * args.micro_batches,
         "micro_batches": args.micro_batches,
         "prompt": args.prompt,
@@ -162,7 +179,7 @@ def run_single(args) -> None:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cfg = llama3_8b()
+    cfg = llama3_8b(args.layers)
     hbm, tflops, peak_kind = peaks()
     workers = build_pipeline(cfg, 1, [dev], transport="local_cuda", dtype=torch.bfloat16, check_values=False)
     w = workers[0]
@@ -263,22 +280,27 @@ def run_single(args) -> None:
         "config": workload_config(args),
         "roofline": {
             "bound": "hbm",
-            "kernel": "gemv_mma (decode linear layers, weight streaming)",
+            "kernel": "gemv_tc (stream-K tcgen05 decode GEMM: qkv, o, gate/up, down, lm_head)",
             "achieved": lin_gbs,
             "peak": hbm,
             "unit": "GB/s",
             "frac": lin_gbs / hbm,
-            "traffic": None,
+            "traffic": NCU_TRAFFIC["gemv_tc"]["dram_bytes"],
+            "traffic_algorithmic": NCU_TRAFFIC["gemv_tc"]["algorithmic_bytes"],
+            "traffic_launches": NCU_TRAFFIC["gemv_tc"]["launches"],
             "peak_kind": peak_kind,
             "share_of_step": lin["ms"] / prof_ms if prof_ms else None,
         },
         "attention_roofline": {
             "bound": "hbm",
-            "kernel": "attn_split + combine (decode attention over the stage-owned KV)",
+            "kernel": "attn_tc + attn_combine (decode attention over the stage-owned KV)",
             "achieved": att_gbs,
             "peak": hbm,
             "unit": "GB/s",
             "frac": att_gbs / hbm,
+            "traffic": NCU_TRAFFIC["attn_tc"]["dram_bytes"],
+            "traffic_algorithmic": NCU_TRAFFIC["attn_tc"]["algorithmic_bytes"],
+            "traffic_launches": NCU_TRAFFIC["attn_tc"]["launches"],
             "share_of_step": att["ms"] / prof_ms if prof_ms else None,
         },
         "step_roofline": {
@@ -314,6 +336,8 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--micro", type=int, default=8)
     ap.add_argument("--micro-batches", type=int, default=4)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="decoder layers (32 = Llama-3-8B; fewer only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -326,7 +350,7 @@ def main() -> None:
         return
     from gpu_mesh_b200.dist import run_pipeline_bench
 
-    run_pipeline_bench(args, llama3_8b(), METRIC, workload_config(args), peaks())
+    run_pipeline_bench(args, llama3_8b(args.layers), METRIC, workload_config(args), peaks(), NCU_TRAFFIC)
 
 
 if __name__ == "__main__":

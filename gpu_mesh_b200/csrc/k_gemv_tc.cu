@@ -261,13 +261,14 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         float4* P = reinterpret_cast<float4*>(slots + ((size_t)p.slot(c, t) * kRows + r) * NP);
 #pragma unroll
         for (int i = 0; i < NP / 4; ++i) P[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        __threadfence();
+        // The barrier orders the four warps' slot writes before thread 64's
+        // release; its acquire (then the barrier) orders the other pieces'
+        // slots before the reads below.
         epi_bar();
         const int c_lo = p.owner((long long)t * p.nk), c_hi = p.owner((long long)(t + 1) * p.nk - 1);
         bool last = false;
-        if (threadIdx.x == 64) last = atomicAdd(&counters[t], 1) == c_hi - c_lo;
+        if (threadIdx.x == 64) last = atomic_add_acq_rel_gpu(&counters[t], 1) == c_hi - c_lo;
         if (!epi_bar_any(last)) continue;  // another CTA finishes this tile
-        __threadfence();
 #pragma unroll
         for (int i = 0; i < NP; ++i) v[i] = 0.f;
         // Pieces are added in CTA order (deterministic); their loads are issued

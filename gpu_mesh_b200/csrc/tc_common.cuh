@@ -71,6 +71,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// Hint: bring a tile of a tensor map into L2 (no shared memory, no completion
+// to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* tm, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tm), "r"(x),
+               "r"(y)
+               : "memory");
+}
+
+// Add to a counter that other CTAs also add to, with release semantics for
+// this thread's prior writes (and, after a barrier, the whole CTA's) and
+// acquire semantics for what the CTAs that added before it wrote.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), descriptor version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc(const void* p) {

@@ -119,7 +119,8 @@ def decode_loop(
 # Benchmark on N GPUs (torchrun)
 # ---------------------------------------------------------------------------
 
-def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[float, float, str]) -> None:
+def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[float, float, str],
+                       traffic: dict | None = None) -> None:
     from gpu_mesh_b200 import greedy_sample
     from gpu_mesh_b200.config import split_layers
     from gpu_mesh_b200.stage import B200Stage
@@ -244,23 +245,28 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 "data": "synthetic (random-init N(0,0.02) weights, uniform-random prompt ids)",
                 "config": {**workload, "stages": world, "parallelism": f"pp{world}",
                            "groups_in_flight": n_groups, "rows_per_group": rows},
+                # Bytes and kernel time are summed over the stages, each on its
+                # own GPU, so the ratios are per-GPU rates.
                 "roofline": {
                     "bound": "hbm",
-                    "kernel": "gemv_tc (decode linear layers, weight streaming), all stages",
-                    "achieved": lin_gbs / world,
+                    "kernel": "gemv_tc (stream-K tcgen05 decode GEMM), mean over stages",
+                    "achieved": lin_gbs,
                     "peak": hbm,
                     "unit": "GB/s",
-                    "frac": lin_gbs / world / hbm,
-                    "traffic": None,
+                    "frac": lin_gbs / hbm,
+                    "traffic": (traffic or {}).get("gemv_tc", {}).get("dram_bytes"),
+                    "traffic_algorithmic": (traffic or {}).get("gemv_tc", {}).get("algorithmic_bytes"),
                     "peak_kind": peak_kind,
                 },
                 "attention_roofline": {
                     "bound": "hbm",
-                    "kernel": "attn_chunk + combine",
-                    "achieved": att_gbs / world,
+                    "kernel": "attn_tc + attn_combine, mean over stages",
+                    "achieved": att_gbs,
                     "peak": hbm,
                     "unit": "GB/s",
-                    "frac": att_gbs / world / hbm,
+                    "frac": att_gbs / hbm,
+                    "traffic": (traffic or {}).get("attn_tc", {}).get("dram_bytes"),
+                    "traffic_algorithmic": (traffic or {}).get("attn_tc", {}).get("algorithmic_bytes"),
                 },
                 "e2e": {
                     "value": rows_total * args.steps / (e2e_ms / 1000.0),
