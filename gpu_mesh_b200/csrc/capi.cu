@@ -227,6 +227,7 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   n_counters = std::max(n_counters, gemv_tc_tiles(st->H, kEpiResid));
   n_counters = std::max(n_counters, gemv_tc_tiles(st->I, kEpiSwiGLU));
   if (st->cfg.has_lm_head) n_counters = std::max(n_counters, gemv_tc_tiles(st->V, kEpiStore));
+  n_counters = std::max(n_counters, (size_t)Mt * st->nkv);  // attention: one per (token, KV head)
   const size_t o_counters = take(n_counters * sizeof(int));
   if (st->work) {
     MG_CUDA(cudaDeviceSynchronize(), "synchronize before work resize");
@@ -472,6 +473,8 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   aa.err = st->err;
   aa.use_tc = 1;
   for (const RowDesc& r : rows) aa.use_tc &= r.kv_tmap != 0;
+  aa.counters = st->counters;
+  aa.counters_elems = st->counters_elems;
 
   const int qd = st->nq * st->D;
   const double norm_bytes = 2.0 * M * H * st->esz;

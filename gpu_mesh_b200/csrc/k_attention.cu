@@ -273,7 +273,9 @@ cudaError_t attn_launch(const AttnArgs& a, dim3 grid, cudaStream_t s) {
 
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys) {
   const int splits = (max_keys + kAttnChunk - 1) / kAttnChunk;
-  return (size_t)M * nq * splits * (D + 2);
+  const size_t simt = (size_t)M * nq * splits * (D + 2);
+  const size_t tc = attention_tc_scratch_elems(nq, D);
+  return simt > tc ? simt : tc;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
@@ -282,12 +284,11 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   const int splits = (a.max_keys + kAttnChunk - 1) / kAttnChunk;
   if (attention_scratch_elems(M, a.nq, a.D, a.max_keys) > a.partial_elems)
     return cudaErrorInvalidValue;
-  dim3 grid(M, a.nkv, splits);
-  cudaError_t e;
   if (a.use_tc && attention_tc_applicable(a.dtype, a.D, a.nq / a.nkv))
-    e = launch_attention_tc(a, grid, s);  // same 128-key chunks and partial format
-  else
-    e = (a.dtype == kBF16) ? attn_launch<__nv_bfloat16>(a, grid, s) : attn_launch<float>(a, grid, s);
+    return launch_attention_tc(a, splits, s);  // merges its chunks itself
+  dim3 grid(M, a.nkv, splits);
+  const cudaError_t e =
+      (a.dtype == kBF16) ? attn_launch<__nv_bfloat16>(a, grid, s) : attn_launch<float>(a, grid, s);
   if (e != cudaSuccess) return e;
   dim3 cgrid(M, a.nq);
   const int threads = a.D < 128 ? a.D : 128;

@@ -5,18 +5,31 @@
 // cores sustain next to the loads, so the dot products run on mma.sync
 // (m16n8k16, bf16 in, fp32 out) with the G heads padded to the MMA's 16 rows.
 //
-// One CTA = one query token x one KV head x a 128-key chunk; each of its 4
-// warps owns 32 keys.  A warp's lane 0 loads its keys and values with 2-D TMA
-// (box 32 keys x 64 dims, 128-byte swizzle, no multicast) through the slot's
-// tensor map, so ldmatrix reads are bank-conflict free; keys arrive on one
-// mbarrier and values on another, so scoring overlaps the value load.
-//   S = Q·Kᵀ   A = Q (heads x dims, registers), B = K rows via ldmatrix
-//   P = exp(S·scale - max)   per head row, quad shuffles
-//   O = P·V    A = P (bf16 hi + lo, from S's accumulators), B = V via ldmatrix.trans
-// The four warps' (max, sum, O) are merged in shared memory into the chunk's
-// partial, which the combine kernel (k_attention.cu) merges across chunks.
-// Every wait is bounded (code 3 in the error word on expiry).
+// Work split (stream-K over keys): the units are (token, KV head, 128-key
+// chunk), and each persistent CTA takes one contiguous run of them, so every
+// SM streams the same number of chunks.  Warp 8 (one lane) loads each chunk's
+// keys and values with 2-D TMA (box 128 keys x 64 dims, 128-byte swizzle, no
+// multicast) through the slot's tensor map, plus the pair's G query rows with
+// a bulk copy, into a 2- or 3-stage ring.  Keys of positions before this
+// forward are not written by the kernels ahead of this one, so for a decode
+// batch (positions implied by the cache length) the producer requests those
+// chunks before its programmatic-launch wait.
+//
+// Warps 0-7 each own 16 keys of every chunk (two warps per scheduler hide the
+// MMA, ldmatrix and exp latencies of each other):
+//   S = Q·Kᵀ   A = Q (heads x dims), B = K rows via ldmatrix
+//   P = exp(S·scale - max)   online over the pair's chunks, quad shuffles
+//   O = O·keep + P·V   A = P (bf16 hi + lo), B = V via ldmatrix.trans
+// At the end of a pair the eight warps' (max, sum, O) are merged in shared
+// memory.  A pair wholly inside the CTA's run is normalised and written to the
+// output; a pair cut by the run's ends leaves an fp32 partial, and the CTA
+// that completes the pair's counter merges the partials in CTA order
+// (deterministic) and writes the output.  Every wait is bounded (code 3 in
+// the error word on expiry); on a timeout the CTA stops, lets the copies it
+// issued land and returns.
 #include <math.h>
+
+#include <algorithm>
 
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -26,10 +39,15 @@ namespace {
 
 using namespace tc;
 
-constexpr int kWarps = 4;
-constexpr int kKeysW = kKvBoxKeys;            // keys per warp (32)
-constexpr int kChunk = kWarps * kKeysW;        // keys per CTA (128)
-constexpr int kBox = kKeysW * 128;             // bytes of one 32 x 64 box
+constexpr int kWarps = 8;                      // consumer warps (two per scheduler)
+constexpr int kThreadsA = (kWarps + 1) * 32;   // + the producer warp
+constexpr int kKeysW = 16;                     // keys per consumer warp
+constexpr int kChunk = kWarps * kKeysW;        // keys per work item (128)
+constexpr int kConsumers = kWarps * 32;
+constexpr int kMaxStages = 3;
+constexpr int kBoxBytes = kKvBoxKeys * 128;    // one 128-key x 64-dim box
+constexpr int kMaxSmem = 227 * 1024;           // dynamic shared memory a CTA may use
+static_assert(kKvBoxKeys == kChunk, "a chunk is one box high");
 
 __device__ __forceinline__ int visible(const AttnArgs& a, const RowDesc& rd, int m, int s) {
   const int total = rd.past + a.S;
@@ -46,6 +64,18 @@ __device__ __forceinline__ void tma_load_2d_gmap(void* dst, uint64_t tmap, uint6
       "%4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
@@ -82,205 +112,435 @@ __device__ __forceinline__ float hi_bf16(uint32_t v) { return __uint_as_float(v 
 // Byte offset of (key row r, 16-byte chunk c of 64 dims) inside a swizzled box.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Barrier over the consumer warps that returns the OR of `pred`, so all of
+// them take the same branch afterwards.
+__device__ __forceinline__ bool consumer_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
+// Shared memory: `stages` ring stages (K, V, Q), the warps' merge area for G
+// heads (m, l, O per warp, then one factor per warp and head, then M and L
+// per head), the barriers.
 template <int D>
 struct TcAttnLayout {
-  static constexpr int kDB = D / 64;                      // 64-dim boxes per key row
-  static constexpr int kWarpKV = 2 * kDB * kBox;           // K and V bytes of one warp
-  static constexpr int kTiles = kWarps * kWarpKV;
-  static constexpr int kMerge = kWarps * 8 * (D + 2) * 4;  // per-warp m, l, O of <= 8 heads
-  static constexpr int kBytes = kTiles + kMerge + 1024 + 256;
+  static constexpr int kDB = D / 64;                       // 64-dim boxes per key row
+  static constexpr int kKV = kDB * kBoxBytes;              // K (or V) bytes of a chunk
+  static constexpr int kQ = 8 * D * 2;                     // <= 8 query heads
+  static constexpr int kStage = (2 * kKV + kQ + 1023) / 1024 * 1024;
+  static constexpr int kBars = 2 * kMaxStages * 8 + 16;
+  __host__ __device__ static constexpr int merge_floats(int G) {
+    return kWarps * G * (D + 2) + kWarps * G + 2 * G;
+  }
+  __host__ __device__ static constexpr int bytes(int stages, int G) {
+    return stages * kStage + (merge_floats(G) * 4 + 15) / 16 * 16 + kBars + 1024;
+  }
+};
+
+// Split of the (token, KV head, chunk) units: pair p = m·nkv + h owns units
+// p·C .. p·C + C - 1 (C = 128-key chunks of the longest row); CTA c takes
+// units [begin(c), begin(c + 1)).  Stream-K ranges are equal; whole-pair
+// ranges end on pair boundaries (chosen when that loses less to imbalance
+// than the cut pairs cost).  A pair inside one CTA's range is finished by
+// that CTA; a pair cut by range ends leaves one partial per CTA in that CTA's
+// slot 0 (its first pair) or 1 (its last), and the CTA that completes the
+// pair's counter merges them in CTA order.
+struct Plan {
+  long long total;  // P·C units
+  long long pairs;  // P
+  int C, grid, whole;
+  __host__ __device__ long long begin(int c) const {
+    return whole ? (long long)c * pairs / grid * C : (long long)c * total / grid;
+  }
+  __host__ __device__ int owner(long long u) const {
+    return whole ? (int)(((u / C + 1) * grid - 1) / pairs) : (int)(((u + 1) * grid - 1) / total);
+  }
+  __host__ __device__ int slot(int c, long long p) const { return 2 * c + (p == begin(c) / C ? 0 : 1); }
 };
 
 template <int D>
-__global__ void __launch_bounds__(kWarps * 32) attn_tc_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan pl, int stages) {
   using L = TcAttnLayout<D>;
   constexpr int DB = L::kDB;
   constexpr int KS = D / 16;  // k-steps of the score MMA
   constexpr int DN = D / 8;   // dim n-tiles of the output
+  const int G = a.nq / a.nkv;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* merge = (float*)(smem + L::kTiles);
-  uint64_t* bars = (uint64_t*)(smem + L::kTiles + L::kMerge);  // [warp][K, V]
+  float* merge = (float*)(smem + stages * L::kStage);  // [warp][head][m, l, O(D)]
+  float* fac = merge + kWarps * G * (D + 2);           // [warp][head]
+  float* mh = fac + kWarps * G;                        // [head] max
+  float* lh = mh + G;                                  // [head] sum
+  uint64_t* full = (uint64_t*)(smem + stages * L::kStage + (L::merge_floats(G) * 4 + 15) / 16 * 16);
+  uint64_t* empty = full + kMaxStages;
+  volatile int* abort_flag = (volatile int*)(empty + kMaxStages);
 
-  pdl_trigger();
-  pdl_wait();
-
-  const int m = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
-  const int G = a.nq / a.nkv;
-  const int bidx = m / a.S, s = m % a.S;
-  const RowDesc rd = a.rows[bidx];
-  const int nvis = visible(a, rd, m, s);
-  const int k0 = sp * kChunk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  float* part = a.partial + ((size_t)(m * a.nkv + h) * gridDim.z + sp) * (size_t)G * (D + 2);
-  if (k0 >= nvis) {
-    for (int i = tid; i < G; i += blockDim.x) {
-      part[i * (D + 2)] = -INFINITY;
-      part[i * (D + 2) + 1] = 0.f;
-    }
-    return;
-  }
+  const int c = blockIdx.x;
+  const long long u0 = pl.begin(c), u1 = pl.begin(c + 1);
+  const int C = pl.C;
+  const uint32_t qbytes = (uint32_t)(G * D * 2);
 
-  const int kw0 = k0 + warp * kKeysW;                   // this warp's first key
-  const int nk = max(0, min(kKeysW, nvis - kw0));        // its visible keys
-  uint8_t* Kw = smem + warp * L::kWarpKV;
-  uint8_t* Vw = Kw + DB * kBox;
-  uint64_t* kbar = bars + 2 * warp;
-  uint64_t* vbar = kbar + 1;
-  if (lane == 0 && nk > 0) {
-    mbar_init(kbar, 1);
-    mbar_init(vbar, 1);
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 2);  // K/V arrival + Q arrival (or a plain arrival)
+      mbar_init(&empty[s], kWarps);
+    }
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const int yk = (int)kv_row(a.layer, 0, rd.slot_rows, rd.row, a.nkv, h, rd.cap, kw0);
-    const int yv = (int)kv_row(a.layer, 1, rd.slot_rows, rd.row, a.nkv, h, rd.cap, kw0);
-    mbar_expect_tx(kbar, DB * kBox);
-    for (int db = 0; db < DB; ++db) tma_load_2d_gmap(Kw + db * kBox, rd.kv_tmap, kbar, db * 64, yk);
-    mbar_expect_tx(vbar, DB * kBox);
-    for (int db = 0; db < DB; ++db) tma_load_2d_gmap(Vw + db * kBox, rd.kv_tmap, vbar, db * 64, yv);
   }
-  __syncwarp();
+  __syncthreads();
+  pdl_trigger();
 
-  // Q fragments (rows = heads g < G, the rest zero), straight from global.
-  uint32_t qa[KS][2];
-  {
-    const __nv_bfloat16* q = (const __nv_bfloat16*)a.q + ((size_t)m * a.nq + (size_t)h * G + g) * D;
+  if (warp == kWarps) {
+    if (lane == 0) {
+      // Producer.  Before its wait it fills at most `stages` stages, and only
+      // with keys of positions that existed before this forward; query rows
+      // (written by the kernel before this one) always come after the wait.
+      bool waited = false;
+      if (a.positions != nullptr) {  // visibility depends on device positions
+        pdl_wait();
+        waited = true;
+      }
+      int qpend[kMaxStages];
+      const __nv_bfloat16* qsrc[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) qpend[s] = 0, qsrc[s] = nullptr;
+      auto issue_q = [&](int s, const __nv_bfloat16* src) {
+        mbar_expect_tx(&full[s], qbytes);
+        bulk_load(smem + s * L::kStage + 2 * L::kKV, src, qbytes, &full[s]);
+      };
+      long long n = 0, cur_p = -1;
+      int m = 0, h = 0, nvis = 0;
+      bool q_done = false;
+      RowDesc rd{};
+      for (long long u = u0; u < u1 && !*abort_flag; ++u) {
+        const long long p = u / C;
+        const int k0 = (int)(u - p * C) * kChunk;
+        if (p != cur_p) {
+          cur_p = p;
+          m = (int)(p / a.nkv);
+          h = (int)(p % a.nkv);
+          rd = a.rows[m / a.S];
+          nvis = visible(a, rd, m, m % a.S);
+          q_done = false;
+        }
+        if (k0 >= nvis) continue;  // consumers skip it too
+        if (!waited && (k0 + kChunk > rd.past || n >= stages)) {
+          pdl_wait();
+          waited = true;
+          for (int s = 0; s < stages; ++s)
+            if (qpend[s]) {
+              issue_q(s, qsrc[s]);
+              qpend[s] = 0;
+            }
+        }
+        const int s = (int)(n % stages);
+        if (n >= stages && !mbar_wait(&empty[s], (int)((n / stages) - 1) & 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * L::kStage;
+        const int yk = (int)kv_row(a.layer, 0, rd.slot_rows, rd.row, a.nkv, h, rd.cap, k0);
+        const int yv = (int)kv_row(a.layer, 1, rd.slot_rows, rd.row, a.nkv, h, rd.cap, k0);
+        mbar_expect_tx(&full[s], 2 * L::kKV);
+        for (int db = 0; db < DB; ++db) tma_load_2d_gmap(st + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yk);
+        for (int db = 0; db < DB; ++db)
+          tma_load_2d_gmap(st + L::kKV + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yv);
+        if (!q_done) {  // the piece's first loaded chunk carries its query rows
+          const __nv_bfloat16* src = (const __nv_bfloat16*)a.q + ((size_t)m * a.nq + (size_t)h * G) * D;
+          if (waited) {
+            issue_q(s, src);
+          } else {
+            qpend[s] = 1;
+            qsrc[s] = src;
+          }
+          q_done = true;
+        } else {
+          mbar_arrive(&full[s]);
+        }
+        ++n;
+      }
+      if (!waited) {
+        pdl_wait();
+        for (int s = 0; s < stages; ++s)
+          if (qpend[s] && !*abort_flag) {
+            issue_q(s, qsrc[s]);
+            qpend[s] = 0;
+          }
+      }
+      if (*abort_flag) {
+        // Complete the arrivals still owed, then let every issued copy land
+        // before shared memory is released.
+        for (int s = 0; s < stages; ++s)
+          if (qpend[s]) mbar_arrive(&full[s]);
+        for (long long i = n > stages ? n - stages : 0; i < n; ++i)
+          mbar_wait(&full[i % stages], (int)(i / stages) & 1, a.err);
+      }
+    }
+  } else {
+    // Consumers: warp w owns keys 16w .. 16w + 15 of each chunk and keeps an
+    // online softmax (max, sum, O) over the chunks of the current pair.
+    pdl_wait();
+    const int g = lane >> 2, t = lane & 3;
+    // Scores are kept in base 2 (scale·log2 e folded in), so every
+    // exponential below is exp2; maxima in the partials are base 2 too.
+    const float scale2 = a.scale * 1.4426950408889634f;
+    long long n = 0;
+    for (long long u = u0; u < u1;) {
+      const long long p = u / C;
+      const long long pe = min(u1, (p + 1) * (long long)C);
+      const int m = (int)(p / a.nkv), h = (int)(p % a.nkv);
+      const RowDesc rd = a.rows[m / a.S];
+      const int nvis = visible(a, rd, m, m % a.S);
+      const int kb = (int)(u - p * C), ke = (int)(pe - p * C);
+      const int kl = min(ke, (nvis + kChunk - 1) / kChunk);  // chunks [kb, kl) hold visible keys
+
+      float mrow = -INFINITY, lrow = 0.f;
+      float o[DN][4];
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
+      for (int i = 0; i < DN; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      uint32_t qa[KS][2];
+      for (int kc = kb; kc < kl; ++kc) {
+        const int s = (int)(n % stages);
+        if (!mbar_wait(&full[s], (int)(n / stages) & 1, a.err)) *abort_flag = 1;
+        ++n;
+        if (*abort_flag) break;  // the vote at the end of the piece stops every warp
+        uint8_t* st = smem + s * L::kStage;
+        uint8_t* Vc = st + L::kKV;
+        if (kc == kb) {
+          const __nv_bfloat16* Qs = (const __nv_bfloat16*)(st + 2 * L::kKV);
+#pragma unroll
+          for (int ks = 0; ks < KS; ++ks) {
+            if (g < G) {
+              qa[ks][0] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 2 * t);
+              qa[ks][1] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 8 + 2 * t);
+            } else {
+              qa[ks][0] = qa[ks][1] = 0u;
+            }
+          }
+        }
+        const int nk = max(0, min(kKeysW, nvis - (kc * kChunk + warp * kKeysW)));
+        if (nk > 0) {
+          // Scores for 16 keys = 2 n-tiles of 8.
+          float sc[2][4];
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+          const uint32_t kbase = smem_u32(st);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int ks = 0; ks < KS; ks += 2) {
+              // four 8x8 matrices: keys 8nt..8nt+7 of this warp, dim chunks 2ks .. 2ks+3
+              const int r = warp * kKeysW + 8 * nt + (lane & 7);
+              const int cc = 2 * ks + (lane >> 3);
+              uint32_t bfr[4];
+              ldsm_x4(kbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), bfr);
+              mma16816(sc[nt], qa[ks][0], qa[ks][1], bfr[0], bfr[1]);
+              mma16816(sc[nt], qa[ks + 1][0], qa[ks + 1][1], bfr[2], bfr[3]);
+            }
+          }
+          // Online softmax of head g (columns 2t, 2t+1 of each n-tile).
+          float mx = mrow;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = 8 * nt + 2 * t + e;
+              const float v = key < nk ? sc[nt][e] * scale2 : -INFINITY;
+              sc[nt][e] = v;
+              mx = fmaxf(mx, v);
+            }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float keep = mrow == -INFINITY ? 0.f : exp2f(mrow - mx);
+          float sum = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float pv = sc[nt][e] == -INFINITY ? 0.f : exp2f(sc[nt][e] - mx);
+              sc[nt][e] = pv;
+              sum += pv;
+            }
+          sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+          mrow = mx;
+          lrow = lrow * keep + sum;
+#pragma unroll
+          for (int i = 0; i < DN; ++i) {
+            o[i][0] *= keep;
+            o[i][1] *= keep;
+          }
+          if (nk < kKeysW) {
+            // Rows past the visible keys hold whatever the cache held (or the
+            // next head's values): P is 0 there, but 0 * NaN is not, so clear them.
+            const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+            for (int i = lane; i < (kKeysW - nk) * DB * 8; i += 32) {
+              const int rr = warp * kKeysW + nk + i / (DB * 8), rem = i % (DB * 8);
+              *reinterpret_cast<uint4*>(Vc + (rem >> 3) * kBoxBytes + rr * 128 + (rem & 7) * 16) = zero;
+            }
+            // The stage is refilled by TMA later: order these writes before it.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+          }
+          // O += P·V over one k-tile of 16 keys.  P = hi + lo, both bf16: two
+          // MMAs keep P to ~2^-17 relative, so the product matches an fp32 P·V.
+          const uint32_t vbase = smem_u32(Vc);
+          const uint32_t pa0 = pack2(sc[0][0], sc[0][1]);
+          const uint32_t pa2 = pack2(sc[1][0], sc[1][1]);
+          const uint32_t pl0 = pack2(sc[0][0] - lo_bf16(pa0), sc[0][1] - hi_bf16(pa0));
+          const uint32_t pl2 = pack2(sc[1][0] - lo_bf16(pa2), sc[1][1] - hi_bf16(pa2));
+#pragma unroll
+          for (int dn = 0; dn < DN; dn += 2) {
+            // matrices: keys +0..7 / +8..15 of this warp, dim chunks dn / dn+1
+            const int mi = lane >> 3;
+            const int r = warp * kKeysW + (lane & 7) + 8 * (mi & 1);
+            const int cc = dn + (mi >> 1);
+            uint32_t bfr[4];
+            ldsm_x4_t(vbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), bfr);
+            mma16816(o[dn], pa0, pa2, bfr[0], bfr[1]);
+            mma16816(o[dn], pl0, pl2, bfr[0], bfr[1]);
+            mma16816(o[dn + 1], pa0, pa2, bfr[2], bfr[3]);
+            mma16816(o[dn + 1], pl0, pl2, bfr[2], bfr[3]);
+          }
+        }
+        // The stage's data is in registers now: hand it back to the producer.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+
+      // End of the piece: merge the warps.
+      float* mw = merge + warp * G * (D + 2);
       if (g < G) {
-        qa[ks][0] = *reinterpret_cast<const uint32_t*>(q + 16 * ks + 2 * t);
-        qa[ks][1] = *reinterpret_cast<const uint32_t*>(q + 16 * ks + 8 + 2 * t);
-      } else {
-        qa[ks][0] = qa[ks][1] = 0u;
-      }
-    }
-  }
-
-  float mrow = -INFINITY, lrow = 0.f;
-  float o[DN][4];
+        if (t == 0) {
+          mw[g * (D + 2)] = mrow;
+          mw[g * (D + 2) + 1] = lrow;
+        }
 #pragma unroll
-  for (int i = 0; i < DN; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  if (nk > 0) {
-    const bool ok_k = mbar_wait(kbar, 0, a.err);
-    // Scores for 32 keys = 4 n-tiles of 8.
-    float sc[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-    const uint32_t kbase = smem_u32(Kw);
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-      for (int ks = 0; ks < KS; ks += 2) {
-        // four 8x8 matrices: keys 8nt..8nt+7, dim chunks 2ks .. 2ks+3
-        const int r = 8 * nt + (lane & 7);
-        const int c = 2 * ks + (lane >> 3);
-        uint32_t bfr[4];
-        ldsm_x4(kbase + (c >> 3) * kBox + swz(r, c & 7), bfr);
-        mma16816(sc[nt], qa[ks][0], qa[ks][1], bfr[0], bfr[1]);
-        mma16816(sc[nt], qa[ks + 1][0], qa[ks + 1][1], bfr[2], bfr[3]);
-      }
-    }
-    // Softmax of head g over this warp's keys (columns 2t, 2t+1 of each n-tile).
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = 8 * nt + 2 * t + e;
-        const float v = (key < nk && ok_k) ? sc[nt][e] * a.scale : -INFINITY;
-        sc[nt][e] = v;
-        mx = fmaxf(mx, v);
-      }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    float sum = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float p = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mx);
-        sc[nt][e] = p;
-        sum += p;
-      }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    mrow = mx;
-    lrow = sum;
-
-    // O = P·V over 2 k-tiles of 16 keys.
-    const bool ok_v = mbar_wait(vbar, 0, a.err);
-    if (nk < kKeysW) {
-      // Rows past the visible keys hold whatever the cache held (or the next
-      // head's values): P is 0 there, but 0 * NaN is not, so clear them.
-      const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-      for (int i = lane; i < (kKeysW - nk) * DB * 8; i += 32) {
-        const int rr = nk + i / (DB * 8), rem = i % (DB * 8);
-        *reinterpret_cast<uint4*>(Vw + (rem >> 3) * kBox + rr * 128 + (rem & 7) * 16) = zero;
-      }
-      __syncwarp();
-    }
-    const uint32_t vbase = smem_u32(Vw);
-#pragma unroll
-    for (int kt = 0; kt < 2; ++kt) {
-      // P = hi + lo, both bf16: two MMAs keep P to ~2^-17 relative, so the
-      // product matches an fp32 P·V instead of a bf16-rounded one.
-      const uint32_t pa0 = pack2(sc[2 * kt][0], sc[2 * kt][1]);
-      const uint32_t pa2 = pack2(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
-      const uint32_t pl0 = pack2(sc[2 * kt][0] - lo_bf16(pa0), sc[2 * kt][1] - hi_bf16(pa0));
-      const uint32_t pl2 = pack2(sc[2 * kt + 1][0] - lo_bf16(pa2), sc[2 * kt + 1][1] - hi_bf16(pa2));
-#pragma unroll
-      for (int dn = 0; dn < DN; dn += 2) {
-        // matrices: keys 16kt+0..7 / +8..15, dim chunks dn / dn+1
-        const int mi = lane >> 3;
-        const int r = 16 * kt + (lane & 7) + 8 * (mi & 1);
-        const int c = dn + (mi >> 1);
-        uint32_t bfr[4];
-        ldsm_x4_t(vbase + (c >> 3) * kBox + swz(r, c & 7), bfr);
-        if (ok_v) {
-          mma16816(o[dn], pa0, pa2, bfr[0], bfr[1]);
-          mma16816(o[dn], pl0, pl2, bfr[0], bfr[1]);
-          mma16816(o[dn + 1], pa0, pa2, bfr[2], bfr[3]);
-          mma16816(o[dn + 1], pl0, pl2, bfr[2], bfr[3]);
+        for (int dn = 0; dn < DN; ++dn) {
+          mw[g * (D + 2) + 2 + 8 * dn + 2 * t] = o[dn][0];
+          mw[g * (D + 2) + 2 + 8 * dn + 2 * t + 1] = o[dn][1];
         }
       }
-    }
-  }
-
-  // Merge the four warps: per head, max, rescaled sum and output.
-  float* mw = merge + warp * 8 * (D + 2);
-  if (g < G && t == 0) {
-    mw[g * (D + 2)] = mrow;
-    mw[g * (D + 2) + 1] = lrow;
-  }
-  if (g < G) {
+      if (consumer_any(*abort_flag)) {  // also orders the writes above
+        *abort_flag = 1;
+        break;
+      }
+      if (tid < G) {
+        float Mx = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) Mx = fmaxf(Mx, merge[(w * G + tid) * (D + 2)]);
+        float Ls = 0.f;
+        for (int w = 0; w < kWarps; ++w) {
+          const float mwv = merge[(w * G + tid) * (D + 2)];
+          const float f = mwv == -INFINITY ? 0.f : exp2f(mwv - Mx);
+          fac[w * G + tid] = f;
+          Ls += f * merge[(w * G + tid) * (D + 2) + 1];
+        }
+        mh[tid] = Mx;
+        lh[tid] = Ls;
+      }
+      consumer_bar();
+      const int c_lo = pl.owner(p * C), c_hi = pl.owner((p + 1) * (long long)C - 1);
+      __nv_bfloat16* out = (__nv_bfloat16*)a.out + ((size_t)m * a.nq + (size_t)h * G) * D;
+      if (c_lo == c_hi) {
+        for (int i = tid; i < G * D; i += kConsumers) {
+          const int hh = i / D, d = i % D;
+          float acc = 0.f;
 #pragma unroll
-    for (int dn = 0; dn < DN; ++dn) {
-      mw[g * (D + 2) + 2 + 8 * dn + 2 * t] = o[dn][0];
-      mw[g * (D + 2) + 2 + 8 * dn + 2 * t + 1] = o[dn][1];
+          for (int w = 0; w < kWarps; ++w) acc += fac[w * G + hh] * merge[(w * G + hh) * (D + 2) + 2 + d];
+          out[i] = __float2bfloat16_rn(acc * (1.0f / lh[hh]));
+        }
+      } else {
+        float* part = a.partial + (size_t)pl.slot(c, p) * G * (D + 2);
+        for (int i = tid; i < G * D; i += kConsumers) {
+          const int hh = i / D, d = i % D;
+          float acc = 0.f;
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) acc += fac[w * G + hh] * merge[(w * G + hh) * (D + 2) + 2 + d];
+          part[hh * (D + 2) + 2 + d] = acc;
+        }
+        if (tid < G) {
+          part[tid * (D + 2)] = mh[tid];
+          part[tid * (D + 2) + 1] = lh[tid];
+        }
+        // The barrier orders the slot writes before thread 0's release; its
+        // acquire (then the barrier) orders the other pieces before the reads.
+        consumer_bar();
+        bool last = false;
+        if (tid == 0) last = atomic_add_acq_rel_gpu(&a.counters[p], 1) == c_hi - c_lo;
+        if (consumer_any(last)) {
+          // Per head: the pieces' maxima give one factor per piece (kept in
+          // the factor area), then every output adds its pieces in CTA order.
+          const int npc = c_hi - c_lo + 1;  // <= grid, so 2·G·npc fits the merge area
+          float* pf = merge;                 // [head][piece] max, then factor
+          float* pls = merge + G * npc;      // [head][piece] sum
+          for (int i = tid; i < G * npc; i += kConsumers) {
+            const int hh = i / npc, k = i % npc;
+            const float* q = a.partial + ((size_t)pl.slot(c_lo + k, p) * G + hh) * (D + 2);
+            pf[i] = __ldcg(q);
+            pls[i] = __ldcg(q + 1);
+          }
+          consumer_bar();
+          if (tid < G) {
+            float Mx = -INFINITY;
+            for (int k = 0; k < npc; ++k) Mx = fmaxf(Mx, pf[tid * npc + k]);
+            float Ls = 0.f;
+            for (int k = 0; k < npc; ++k) {
+              const float mk = pf[tid * npc + k];
+              const float f = mk == -INFINITY ? 0.f : exp2f(mk - Mx);
+              Ls += f * pls[tid * npc + k];
+              pf[tid * npc + k] = f;
+            }
+            lh[tid] = Ls;
+          }
+          consumer_bar();
+          for (int i = tid; i < G * D; i += kConsumers) {
+            const int hh = i / D, d = i % D;
+            float acc = 0.f;
+            for (int k0 = 0; k0 < npc; k0 += 8) {
+              float v[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k)  // eight independent loads in flight
+                v[k] = k0 + k < npc
+                           ? __ldcg(a.partial + ((size_t)pl.slot(c_lo + k0 + k, p) * G + hh) * (D + 2) + 2 + d)
+                           : 0.f;
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                if (k0 + k < npc) acc += pf[hh * npc + k0 + k] * v[k];
+            }
+            out[i] = __float2bfloat16_rn(acc * (1.0f / lh[hh]));
+          }
+          if (tid == 0) a.counters[p] = 0;
+        }
+      }
+      consumer_bar();  // the merge area is rewritten by the next piece
+      u = pe;
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * (D + 1); i += blockDim.x) {
-    const int hh = i / (D + 1), d = i % (D + 1);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[w * 8 * (D + 2) + hh * (D + 2)]);
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float mwv = merge[w * 8 * (D + 2) + hh * (D + 2)];
-      if (mwv == -INFINITY) continue;
-      const float f = expf(mwv - M);
-      acc += f * merge[w * 8 * (D + 2) + hh * (D + 2) + (d == D ? 1 : 2 + d)];
-    }
-    if (d == D) {
-      part[hh * (D + 2)] = M;
-      part[hh * (D + 2) + 1] = acc;
-    } else {
-      part[hh * (D + 2) + 2 + d] = acc;
-    }
+}
+
+int sm_count_attn() {
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
   }
+  return n[dev];
 }
 
 }  // namespace
@@ -289,24 +549,61 @@ bool attention_tc_applicable(int dtype, int D, int G) {
   return dtype == kBF16 && (D == 64 || D == 128) && G <= 8;
 }
 
-size_t attention_tc_chunk() { return kChunk; }
+size_t attention_tc_scratch_elems(int nq, int D) {
+  // Two partial slots per CTA, at most two CTAs per SM, G <= 8 heads each.
+  return (size_t)2 * 2 * sm_count_attn() * (size_t)(nq < 8 ? nq : 8) * (D + 2);
+}
 
-cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s) {
-  auto go = [&](auto kernel, int smem) -> cudaError_t {
+cudaError_t launch_attention_tc(const AttnArgs& a, int splits, cudaStream_t s) {
+  if ((uintptr_t)a.q % 16) return cudaErrorInvalidValue;
+  const long long pairs = (long long)a.B * a.S * a.nkv;
+  if (pairs <= 0) return cudaSuccess;
+  if (!a.counters || a.counters_elems < (size_t)pairs) return cudaErrorInvalidValue;
+  const int G = a.nq / a.nkv;
+  auto go = [&](auto kernel, int smem, int stages) -> cudaError_t {
     static bool configured[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     bool& done = configured[a.D == 128][dev];
     if (!done) {
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
       if (e != cudaSuccess) return e;
       done = true;
     }
-    return launch_pdl(kernel, grid, dim3(kWarps * 32), smem, s, a);
+    static int per_sm_cache[2][9][64] = {};  // [D == 128][G][device]
+    int& per_sm = per_sm_cache[a.D == 128][G][dev];
+    if (!per_sm) {
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreadsA, smem);
+      if (e != cudaSuccess) return e;
+      per_sm = n > 0 ? (n < 2 ? n : 2) : 1;
+    }
+    Plan pl;
+    pl.C = splits;
+    pl.pairs = pairs;
+    pl.total = pairs * splits;
+    // A cut pair's pieces (at most one per CTA) are merged through the merge
+    // area, which holds 4·(D + 2) pieces per head.
+    const long long cap = std::min<long long>((long long)sm_count_attn() * per_sm, 4 * (a.D + 2));
+    // Whole pairs when the busiest CTA then streams no more chunks than an
+    // equal stream-K range plus what its cut pairs cost (about 4 chunks).
+    const long long whole_span = (pairs + cap - 1) / cap * splits;
+    const long long sk_span = (pl.total + cap - 1) / cap + 4;
+    pl.whole = whole_span <= sk_span;
+    const long long units = pl.whole ? pairs : pl.total;
+    pl.grid = (int)(units < cap ? units : cap);
+    if ((size_t)2 * pl.grid * G * (a.D + 2) > a.partial_elems) return cudaErrorInvalidValue;
+    return launch_pdl(kernel, dim3(pl.grid), dim3(kThreadsA), smem, s, a, pl, stages);
   };
-  if (a.D == 128) return go(attn_tc_kernel<128>, TcAttnLayout<128>::kBytes);
-  return go(attn_tc_kernel<64>, TcAttnLayout<64>::kBytes);
+  // Three stages where they fit next to the merge area, else two.
+  if (a.D == 128) {
+    using L = TcAttnLayout<128>;
+    const int stages = L::bytes(3, G) <= kMaxSmem ? 3 : 2;
+    return go(attn_tc_kernel<128>, L::bytes(stages, G), stages);
+  }
+  using L = TcAttnLayout<64>;
+  return go(attn_tc_kernel<64>, L::bytes(3, G), 3);
 }
 
 }  // namespace mg

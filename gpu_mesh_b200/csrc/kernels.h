@@ -45,7 +45,7 @@ struct RowDesc {
 // The KV tensor map of a slot views its block as a 2-D bf16 array
 // [layers*2*rows*nkv*cap, D] with a box of kKvBoxKeys keys x 64 dims and a
 // 128-byte swizzle; kv_row() is the row of (layer, K|V, row, head, pos).
-constexpr int kKvBoxKeys = 32;
+constexpr int kKvBoxKeys = 128;
 __host__ __device__ inline int64_t kv_row(int layer, int kv, int slot_rows, int row, int nkv,
                                           int head, int cap, int pos) {
   return ((((int64_t)(layer * 2 + kv) * slot_rows + row) * nkv + head) * cap + pos);
@@ -129,13 +129,21 @@ struct AttnArgs {
   float scale;
   int* err;                 // stage error word (bounded-wait timeouts)
   int use_tc;               // every row has a KV tensor map: tensor-core kernel
+  // Per-(token, KV head) counters of the tensor-core kernel: zero when a
+  // launch starts and zero again when it ends.
+  int* counters;
+  size_t counters_elems;
 };
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
-// Tensor-core attention (k_attention_tc.cu): bf16, head_dim 64 or 128, G <= 8.
+// Tensor-core attention (k_attention_tc.cu): bf16, head_dim 64 or 128, G <= 8;
+// `splits` 128-key chunks per (token, KV head) of the longest row.  It writes
+// `out` itself (no combine launch); its fp32 scratch need is
+// attention_tc_scratch_elems, its counters one per (token, KV head).
 bool attention_tc_applicable(int dtype, int D, int G);
-cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s);
+size_t attention_tc_scratch_elems(int nq, int D);
+cudaError_t launch_attention_tc(const AttnArgs& a, int splits, cudaStream_t s);
 
 cudaError_t launch_argmax(int dtype, const void* logits, int rows, int vocab, int64_t row_stride,
                           int64_t* ids, cudaStream_t s);
