@@ -26,100 +26,14 @@
 // previous kernel.  Every wait is bounded; on a timeout the
 // kernel records code 3 in the error word, drains what it issued, frees its
 // TMEM and returns.
+#include "gemv_tc_parts.cuh"
 #include "linear_tc.h"
-#include "tc_common.cuh"
 
 namespace mg {
 namespace {
 
 using namespace tc;
-using bf16 = __nv_bfloat16;
-
-constexpr int kRows = 128;
-constexpr int kKB = 64;
-constexpr int kStagesD = 8;  // 144-160 KB of weights in flight per SM
-constexpr int kThreadsD = 192;
-constexpr int kWBytes = kRows * kKB * 2;
-
-template <int NP>
-struct DLayout {
-  static constexpr int kX = NP * kKB * 2;
-  static constexpr int kStage = kWBytes + kX;  // a multiple of 1024
-  static constexpr int kTiles = kStagesD * kStage;
-  static constexpr int kXchg = 64 * NP * 4;
-  static constexpr int kBytes = kTiles + kXchg + 1024 + 512;
-};
-
-struct Part {
-  long long total;  // units
-  int G, nk, tiles;
-  __host__ __device__ long long begin(int c) const { return (long long)c * total / G; }
-  __host__ __device__ int owner(long long u) const { return (int)(((u + 1) * G - 1) / total); }
-  __host__ __device__ int slot(int c, int t) const { return 2 * c + (t == begin(c) / nk ? 0 : 1); }
-};
-
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Barrier over the four epilogue warps that also returns the OR of `pred`
-// across them, so every warp takes the same branch afterwards.
-__device__ __forceinline__ bool epi_bar_any(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "barrier.red.or.pred q, 1, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred)
-      : "memory");
-  return r != 0;
-}
-
-template <int NP, int EPI>
-__device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const float* v, float* xchg) {
-  if (EPI == kEpiSwiGLU) {
-    // rows 0-63 gate, 64-127 up of features 64t .. 64t+63
-    if (r >= 64) {
-#pragma unroll
-      for (int i = 0; i < NP; ++i) xchg[(r - 64) * NP + i] = v[i];
-    }
-    epi_bar();
-    if (r < 64) {
-      const int f = t * 64 + r;
-      if (f < a.N) {
-        bf16* Y = (bf16*)a.Y + f;
-#pragma unroll
-        for (int tok = 0; tok < NP; ++tok) {
-          if (tok >= a.M) break;
-          const float g = rt<bf16>(v[tok]), u = rt<bf16>(xchg[r * NP + tok]);
-          const float sg = rt<bf16>(g / (1.0f + expf(-g)));
-          Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(sg * u);
-        }
-      }
-    }
-    epi_bar();
-    return;
-  }
-  const int f = t * kRows + r;
-  if (f >= a.N) return;
-  bf16* Y = (bf16*)a.Y + f;
-  if (EPI == kEpiResid) {
-    // R may alias Y, so the compiler cannot hoist a load above the previous
-    // token's store: read every residual first, then write.
-    const bf16* R = (const bf16*)a.R + f;
-    float rr[NP];
-#pragma unroll
-    for (int tok = 0; tok < NP; ++tok)
-      rr[tok] = tok < a.M ? __bfloat162float(R[(size_t)tok * a.ldr]) : 0.f;
-#pragma unroll
-    for (int tok = 0; tok < NP; ++tok)
-      if (tok < a.M) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(rr[tok] + rt<bf16>(v[tok]));
-  } else {
-#pragma unroll
-    for (int tok = 0; tok < NP; ++tok)
-      if (tok < a.M) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(v[tok]);
-  }
-}
+using namespace gemvtc;
 
 template <int NP, int EPI>
 __global__ void __launch_bounds__(kThreadsD, 1)
@@ -129,7 +43,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* xchg = (float*)(smem + L::kTiles);
-  uint64_t* full = (uint64_t*)(smem + L::kTiles + L::kXchg);
+  uint64_t* full = (uint64_t*)(smem + L::kBarOff);
   uint64_t* empty = full + kStagesD;
   uint64_t* tfull = empty + kStagesD;    // [2]
   uint64_t* tempty = tfull + 2;          // [2]
@@ -242,11 +156,16 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     pdl_wait();
     const int q = warp & 3;
     const int r = q * 32 + lane;  // W row within the tile
+    const int e = threadIdx.x - 64;
     int pi = 0;
+    bool ok = true;
     for (int t = t_first; t <= t_last; ++t, ++pi) {
       const int b = pi & 1;
-      const bool ok = mbar_wait(&tfull[b], (pi >> 1) & 1, err);
-      if (epi_bar_any(!ok)) break;  // a timeout anywhere stops all four warps together
+      ok = mbar_wait(&tfull[b], (pi >> 1) & 1, err);
+      if (epi_bar_any(!ok)) {  // a timeout anywhere stops all four warps together
+        ok = false;
+        break;
+      }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       float v[NP];
       __syncwarp();
@@ -257,49 +176,10 @@ __global__ void __launch_bounds__(kThreadsD, 1)
 
       const long long lo = max(u0, (long long)t * p.nk), hi = min(u1, (long long)(t + 1) * p.nk);
       const bool whole = lo == (long long)t * p.nk && hi == (long long)(t + 1) * p.nk;
-      if (!whole) {
-        float4* P = reinterpret_cast<float4*>(slots + ((size_t)p.slot(c, t) * kRows + r) * NP);
-#pragma unroll
-        for (int i = 0; i < NP / 4; ++i) P[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        // The barrier orders the four warps' slot writes before thread 64's
-        // release; its acquire (then the barrier) orders the other pieces'
-        // slots before the reads below.
-        epi_bar();
-        const int c_lo = p.owner((long long)t * p.nk), c_hi = p.owner((long long)(t + 1) * p.nk - 1);
-        bool last = false;
-        if (threadIdx.x == 64) last = atomic_add_acq_rel_gpu(&counters[t], 1) == c_hi - c_lo;
-        if (!epi_bar_any(last)) continue;  // another CTA finishes this tile
-#pragma unroll
-        for (int i = 0; i < NP; ++i) v[i] = 0.f;
-        // Pieces are added in CTA order (deterministic); their loads are issued
-        // kBatch pieces at a time so the L2 round trips overlap.
-        constexpr int kBatch = NP == 16 ? 4 : 2;
-        for (int c0 = c_lo; c0 <= c_hi; c0 += kBatch) {
-          float4 buf[kBatch][NP / 4];
-#pragma unroll
-          for (int b2 = 0; b2 < kBatch; ++b2) {
-            if (c0 + b2 > c_hi) break;
-            const float4* S =
-                reinterpret_cast<const float4*>(slots + ((size_t)p.slot(c0 + b2, t) * kRows + r) * NP);
-#pragma unroll
-            for (int i = 0; i < NP / 4; ++i) buf[b2][i] = __ldcg(S + i);
-          }
-#pragma unroll
-          for (int b2 = 0; b2 < kBatch; ++b2) {
-            if (c0 + b2 > c_hi) break;
-#pragma unroll
-            for (int i = 0; i < NP / 4; ++i) {
-              v[4 * i] += buf[b2][i].x;
-              v[4 * i + 1] += buf[b2][i].y;
-              v[4 * i + 2] += buf[b2][i].z;
-              v[4 * i + 3] += buf[b2][i].w;
-            }
-          }
-        }
-        if (threadIdx.x == 64) counters[t] = 0;
-      }
+      if (!whole && !piece_done<NP>(p, slots, counters, c, t, r, e, v)) continue;  // another CTA finishes it
       apply<NP, EPI>(a, t, r, v, xchg);
     }
+    if (!ok) *abort_flag = 1;
   }
 
   __syncthreads();
@@ -317,34 +197,11 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   }
 }
 
-int sm_count() {
-  static int n[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!n[dev]) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    n[dev] = v > 0 ? v : 148;
-  }
-  return n[dev];
-}
-
-Part make_part(int M, int N, int K, int epi) {
-  Part p;
-  p.tiles = (epi == kEpiSwiGLU) ? (N + 63) / 64 : (N + kRows - 1) / kRows;
-  p.nk = K / kKB;
-  p.total = (long long)p.tiles * p.nk;
-  p.G = (int)std::min<long long>(sm_count(), p.total);
-  (void)M;
-  return p;
-}
-
 size_t counters_elems(const Part& p) { return ((size_t)p.tiles + 63) / 64 * 64; }
 
 template <int NP, int EPI>
 cudaError_t launch(const LinearArgs& a, cudaStream_t s) {
-  const Part p = make_part(a.M, a.N, a.K, a.epilogue);
+  const Part p = make_part(a.N, a.K, a.epilogue);
   int* counters = a.counters;
   float* slots = a.partial;
   size_t slot_elems = a.partial_elems;
@@ -392,7 +249,7 @@ bool gemv_tc_applicable(int dtype, int M, int N, int K) {
 }
 
 size_t gemv_tc_scratch_elems(int M, int N, int K, int epilogue, bool with_counters) {
-  const Part p = make_part(M, N, K, epilogue);
+  const Part p = make_part(N, K, epilogue);
   const int np = M <= 16 ? 16 : 32;
   return (with_counters ? counters_elems(p) : 0) + (size_t)2 * p.G * kRows * np;
 }

@@ -49,11 +49,38 @@ __global__ void __launch_bounds__(kSampleThreads) argmax_kernel(const T* __restr
   const T* row = logits + (size_t)blockIdx.x * stride;
   float bv = -INFINITY;
   int bi = INT_MAX;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = logit_at<T>(row, i);
-    if (better(v, i, bv, bi)) {
-      bv = v;
-      bi = i;
+  constexpr int VEC = Vec16<T>::N;
+  if ((vocab % VEC) == 0 && ((uintptr_t)row % 16) == 0) {
+    // 16-byte vectors, two in flight per thread; indices within a thread
+    // only grow, so keeping the first of equal values keeps the lowest index.
+    const int nv = vocab / VEC;
+    for (int i = threadIdx.x; i < nv; i += 2 * blockDim.x) {
+      float v0[VEC], v1[VEC];
+      const int i1 = i + blockDim.x;
+      load16_f<T>(row + (size_t)i * VEC, v0);
+      if (i1 < nv) load16_f<T>(row + (size_t)i1 * VEC, v1);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        if (better(v0[j], i * VEC + j, bv, bi)) {
+          bv = v0[j];
+          bi = i * VEC + j;
+        }
+      if (i1 < nv) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          if (better(v1[j], i1 * VEC + j, bv, bi)) {
+            bv = v1[j];
+            bi = i1 * VEC + j;
+          }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+      const float v = logit_at<T>(row, i);
+      if (better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
     }
   }
 #pragma unroll
