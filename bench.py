@@ -170,6 +170,68 @@ def workload_config(args) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Long-context decode attention (one of eight 4-layer stages)
+# ---------------------------------------------------------------------------
+
+def long_context(hbm: float, *, rows: int = 64, context: int = 8192, layers: int = 4, steps: int = 8) -> dict:
+    """Decode through one middle stage of the Llama-3-8B geometry (4 layers,
+    what each GPU of an 8-stage pipeline holds) for 64 rows whose KV caches
+    are pre-filled to 8192 positions with N(0, 1) values: attention streams
+    2.15 GB of keys and values per layer per step against 0.44 GB of weights.
+    Returns decode tok/s of the stage and the attention kernels' HBM rate
+    from the per-launch CUDA events."""
+    from gpu_mesh_b200 import B200Stage
+    from gpu_mesh_b200.weights import synthetic_stage_state
+
+    cfg = llama3_8b(layers)
+    cfg.max_position_embeddings = context + 2 * steps + 64  # the cache plus the decoded tokens
+    dev = torch.device("cuda", 0)
+    state = synthetic_stage_state(cfg, 0, layers, has_embedding=False, has_lm_head=False, seed=0,
+                                  dtype=torch.bfloat16, device=dev)
+    stage = B200Stage(cfg, 0, layers, has_embedding=False, has_lm_head=False, device=dev,
+                      dtype=torch.bfloat16, state_dict=state)
+    del state
+    g = torch.Generator(device=dev).manual_seed(5)
+    nkv, D = cfg.num_key_value_heads, cfg.head_dim
+    stage.kv_reserve(0, rows, context + steps + 8)
+    for layer in range(layers):
+        k = torch.randn(rows, nkv, context, D, generator=g, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(rows, nkv, context, D, generator=g, device=dev, dtype=torch.bfloat16)
+        stage.kv_import(0, layer, k, v)
+        del k, v
+    x = (torch.randn(rows, 1, cfg.hidden_size, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    for _ in range(2):  # warm-up
+        stage.forward_slot(0, x)
+    stage.kv_trim(0, context)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        stage.forward_slot(0, x)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    stage.kv_trim(0, context)
+    stage.profile(True)
+    for _ in range(steps):
+        stage.forward_slot(0, x)
+    prof = stage.profile_read()
+    stage.profile(False)
+    stage.close()
+    att = prof["attention"]
+    att_gbs = att["bytes"] / (att["ms"] / 1000.0) / 1e9 if att["ms"] else 0.0
+    return {
+        "workload": (f"one middle stage of 4 Llama-3-8B layers, {rows} rows, KV pre-filled to {context} "
+                     "positions with N(0,1), single-token decode"),
+        "stage_tok_s": rows / (ms / 1000.0),
+        "ms_per_step": ms,
+        "attention": {"achieved": att_gbs, "peak": hbm, "unit": "GB/s", "frac": att_gbs / hbm,
+                      "bytes_per_step": att["bytes"] / steps, "share_of_step": att["ms"] / sum(
+                          p["ms"] for p in prof.values())},
+    }
+
+
+# ---------------------------------------------------------------------------
 # B200 arm, one GPU
 # ---------------------------------------------------------------------------
 
@@ -260,6 +322,15 @@ def run_single(args) -> None:
     step_bytes = sum(p["bytes"] for p in prof.values()) / args.steps
     prof_ms = sum(p["ms"] for p in prof.values())
 
+    # Free the 8B stage before the long-context stage.
+    for k in keys:
+        w.clear_kv(k)
+    for wk in workers:
+        wk.close()
+    del workers, w, stage
+    torch.cuda.empty_cache()
+    longctx = None if args.no_long_context else long_context(hbm)
+
     base = None
     if not args.no_cpu_baseline:
         base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=2)
@@ -322,6 +393,8 @@ def run_single(args) -> None:
         "profile": prof,
         "clocks": clocks.summary(),
     }
+    if longctx is not None:
+        line["long_context"] = longctx
     if base is not None:
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line), flush=True)
@@ -330,7 +403,7 @@ def run_single(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--prompt", type=int, default=1024)
@@ -339,6 +412,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=32,
                     help="decoder layers (32 = Llama-3-8B; fewer only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long-context", action="store_true",
+                    help="skip the long-context attention measurement (64 rows x 8192 positions)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
