@@ -201,7 +201,12 @@ size_t scratch_needed(const mg_stage* st, int M, int rows, int max_keys) {
     s = std::max(s, linear_scratch_elems(dt, rows, st->V, st->H, kEpiStore));
   }
   s = std::max(s, attention_scratch_elems(M, st->nq, st->D, max_keys));
-  if (M <= 32) s = std::max(s, layer_chain_scratch_elems());
+  if (M <= 32) {
+    s = std::max(s, layer_chain_scratch_elems());
+    s = std::max(s, linear_scratch_elems(dt, M, st->Nqkv, st->H, kEpiPieces));
+    s = std::max(s, linear_scratch_elems(dt, M, st->H, st->nq * st->D, kEpiPieces));
+    s = std::max(s, linear_scratch_elems(dt, M, st->H, st->I, kEpiPieces));
+  }
   return s;
 }
 
@@ -509,6 +514,7 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   ca.err = st->err;
   ca.bar = st->chain_bar;
   bool lm_in_chain = false;
+  bool final_norm_done = false;  // the last residual kernel also ran the final norm
   auto chain_linear = [&](ChainStep& cs, const void* X, int64_t ldx, const void* W, void* Y, int64_t ldy,
                           const void* R, int64_t ldr, int N, int K, int epi) {
     cs.kind = kChainLinear;
@@ -593,30 +599,58 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
                             (unsigned)(ca.nsteps - 1) * (unsigned)layer_chain_grid());  // wraps like the device word
     }
   } else {
+    // Decode rows on the tcgen05 GEMM: the qkv, o_proj and down projections
+    // leave their fp32 pieces, and the kernel after each (RoPE / append, or
+    // the residual add + RMSNorm) adds them, so no GEMM ends in a fix-up.
+    Pieces pq{}, po{}, pd{};
+    const bool use_pieces = M <= 32 && gemv_pieces_plan(dt, M, st->Nqkv, H, &pq) &&
+                            gemv_pieces_plan(dt, M, H, qd, &po) && gemv_pieces_plan(dt, M, H, st->I, &pd);
+    pq.slots = po.slots = pd.slots = st->part;
+    const double resid_bytes = 3.0 * M * H * st->esz;  // residual in and out, normalised row out
     for (int l = 0; l < st->L; ++l) {
       const LayerW& w = st->layers[l];
-      MG_TIMED(MG_PROF_OTHER, norm_bytes, 0, launch_rmsnorm(dt, st->x, H, w.ln1, M, H, c.rms_norm_eps, st->xn, s), "input_layernorm");
+      if (l == 0 || !use_pieces)
+        MG_TIMED(MG_PROF_OTHER, norm_bytes, 0, launch_rmsnorm(dt, st->x, H, w.ln1, M, H, c.rms_norm_eps, st->xn, s), "input_layernorm");
       la.X = st->xn; la.ldx = H; la.W = w.wqkv; la.Y = st->qkv; la.ldy = st->Nqkv;
-      la.N = st->Nqkv; la.K = H; la.epilogue = kEpiStore; la.R = nullptr;
+      la.N = st->Nqkv; la.K = H; la.epilogue = use_pieces ? kEpiPieces : kEpiStore; la.R = nullptr;
       MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "qkv projection");
       qa.layer = l;
       qa.q_norm = w.qn;
       qa.k_norm = w.kn;
+      qa.use_pieces = use_pieces;
+      qa.pieces = pq;
       MG_TIMED(MG_PROF_OTHER, 2.0 * M * st->Nqkv * st->esz, 0, launch_qkv_post(qa, s), "rope / kv append");
       aa.layer = l;
       MG_TIMED(MG_PROF_ATTENTION, attn_bytes, attn_flops, launch_attention(aa, s), "attention");
       la.X = st->attn; la.ldx = qd; la.W = w.wo; la.Y = st->x; la.ldy = H;
-      la.N = H; la.K = qd; la.epilogue = kEpiResid; la.R = st->x; la.ldr = H;
+      la.N = H; la.K = qd; la.epilogue = use_pieces ? kEpiPieces : kEpiResid; la.R = st->x; la.ldr = H;
       MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "o_proj");
-      MG_TIMED(MG_PROF_OTHER, norm_bytes, 0,
-               launch_rmsnorm(dt, st->x, H, w.ln2, M, H, c.rms_norm_eps, st->xn, s),
-               "post_attention_layernorm");
+      if (use_pieces)
+        MG_TIMED(MG_PROF_OTHER, resid_bytes, 0,
+                 launch_resid_norm_pieces(dt, po, st->x, w.ln2, st->xn, M, H, c.rms_norm_eps, s),
+                 "o_proj residual + post_attention_layernorm");
+      else
+        MG_TIMED(MG_PROF_OTHER, norm_bytes, 0,
+                 launch_rmsnorm(dt, st->x, H, w.ln2, M, H, c.rms_norm_eps, st->xn, s),
+                 "post_attention_layernorm");
       la.X = st->xn; la.ldx = H; la.W = w.wgu; la.Y = st->h; la.ldy = st->I;
       la.N = st->I; la.K = H; la.epilogue = kEpiSwiGLU; la.R = nullptr;
       MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "gate/up projection");
       la.X = st->h; la.ldx = st->I; la.W = w.wd; la.Y = st->x; la.ldy = H;
-      la.N = H; la.K = st->I; la.epilogue = kEpiResid; la.R = st->x; la.ldr = H;
+      la.N = H; la.K = st->I; la.epilogue = use_pieces ? kEpiPieces : kEpiResid; la.R = st->x; la.ldr = H;
       MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "down_proj");
+      if (use_pieces) {
+        const void* nw = nullptr;
+        if (l + 1 < st->L) {
+          nw = st->layers[l + 1].ln1;
+        } else if (c.has_lm_head && rows_out == M) {
+          nw = st->norm;
+          final_norm_done = true;
+        }
+        MG_TIMED(MG_PROF_OTHER, resid_bytes, 0,
+                 launch_resid_norm_pieces(dt, pd, st->x, nw, st->xn, M, H, c.rms_norm_eps, s),
+                 "down_proj residual + next norm");
+      }
     }
   }
 
@@ -626,9 +660,10 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
     const void* src = last_only ? (const void*)((const char*)st->x + (size_t)(S - 1) * H * st->esz)
                                 : st->x;
     const int64_t stride = last_only ? (int64_t)S * H : H;
-    MG_TIMED(MG_PROF_OTHER, 2.0 * rows_out * H * st->esz, 0,
-             launch_rmsnorm(dt, src, stride, st->norm, rows_out, H, c.rms_norm_eps, st->xn, s),
-             "final norm");
+    if (!final_norm_done)
+      MG_TIMED(MG_PROF_OTHER, 2.0 * rows_out * H * st->esz, 0,
+               launch_rmsnorm(dt, src, stride, st->norm, rows_out, H, c.rms_norm_eps, st->xn, s),
+               "final norm");
     la.M = rows_out;
     la.X = st->xn; la.ldx = H; la.W = st->lm_head; la.Y = out; la.ldy = st->V;
     la.N = st->V; la.K = H; la.epilogue = kEpiStore; la.R = nullptr;

@@ -67,6 +67,46 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __r
   }
 }
 
+// The residual epilogue of a decode GEMM left as pieces, then (optionally)
+// the RMSNorm of the new residual row: thread j owns 8-element vectors j,
+// j + 128, ... as in rmsnorm_kernel at 128 threads, so the sum of squares is
+// added in the same order.
+__global__ void __launch_bounds__(128) resid_norm_pieces_kernel(Pieces pc, __nv_bfloat16* __restrict__ x,
+                                                                const __nv_bfloat16* __restrict__ w, int H,
+                                                                float eps, __nv_bfloat16* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  __nv_bfloat16* xr = x + (size_t)m * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+    float acc[8], v[8];
+    pieces_sum8(pc, m, i * 8, acc);
+    load16_f<__nv_bfloat16>(xr + i * 8, v);
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o[j] = __float2bfloat16_rn(v[j] + rt<__nv_bfloat16>(acc[j]));
+      const float nv = __bfloat162float(o[j]);
+      ss += nv * nv;
+    }
+    *reinterpret_cast<uint4*>(xr + i * 8) = *reinterpret_cast<const uint4*>(o);
+  }
+  if (!w) return;
+  ss = block_sum<__nv_bfloat16>(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)H + eps);
+  __nv_bfloat16* yr = y + (size_t)m * H;
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+    float v[8], g[8];
+    load16_f<__nv_bfloat16>(xr + i * 8, v);  // this thread's own stores
+    load16_f<__nv_bfloat16>(w + i * 8, g);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      stf<__nv_bfloat16>(yr + i * 8 + j, rt<__nv_bfloat16>(rt<__nv_bfloat16>(v[j] * r) * g[j]));
+  }
+}
+
 template <typename T>
 __global__ void kv_copy_kernel(T* __restrict__ kv, int layer, int kvsel, int slot_rows, int nkv,
                                int cap, int D, int len, T* __restrict__ ext, bool to_slot) {
@@ -92,6 +132,15 @@ cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M
                                                   (__nv_bfloat16*)out, err); if (_le != cudaSuccess) return _le; }
   else
     { const cudaError_t _le = launch_pdl(embed_kernel<float>, dim3(M), dim3(128), 0, s, (const float*)table, ids, H, V, (float*)out, err); if (_le != cudaSuccess) return _le; }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const void* w, void* xn, int M,
+                                     int H, float eps, cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  if (dtype != kBF16 || H % 8 || !pc.slots) return cudaErrorInvalidValue;
+  { const cudaError_t _le = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(128), 0, s, pc, (__nv_bfloat16*)x,
+                                        (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -174,6 +174,13 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&tempty[b])) : "memory");
 
+      if (EPI == kEpiPieces) {  // leave the sums for the consuming kernel
+        float* S = slots + (size_t)(c + t) * NP * kRows + r;
+#pragma unroll
+        for (int tok = 0; tok < NP; ++tok)
+          if (tok < a.M) S[tok * kRows] = v[tok];
+        continue;
+      }
       const long long lo = max(u0, (long long)t * p.nk), hi = min(u1, (long long)(t + 1) * p.nk);
       const bool whole = lo == (long long)t * p.nk && hi == (long long)(t + 1) * p.nk;
       if (!whole && !piece_done<NP>(p, slots, counters, c, t, r, e, v)) continue;  // another CTA finishes it
@@ -215,7 +222,8 @@ cudaError_t launch(const LinearArgs& a, cudaStream_t s) {
   } else if (a.counters_elems < (size_t)p.tiles) {
     return cudaErrorInvalidValue;
   }
-  if (!slots || slot_elems < (size_t)2 * p.G * kRows * NP) return cudaErrorInvalidValue;
+  const size_t nslots = EPI == kEpiPieces ? (size_t)p.G + p.tiles : (size_t)2 * p.G;
+  if (!slots || slot_elems < nslots * kRows * NP) return cudaErrorInvalidValue;
   CUtensorMap tw, tx;
   const uint64_t wrows = (EPI == kEpiSwiGLU) ? 2ull * a.N : (uint64_t)a.N;
   if (!tc_host::make_map(&tw, a.W, wrows, a.K, a.K, 64) ||
@@ -251,7 +259,19 @@ bool gemv_tc_applicable(int dtype, int M, int N, int K) {
 size_t gemv_tc_scratch_elems(int M, int N, int K, int epilogue, bool with_counters) {
   const Part p = make_part(N, K, epilogue);
   const int np = M <= 16 ? 16 : 32;
-  return (with_counters ? counters_elems(p) : 0) + (size_t)2 * p.G * kRows * np;
+  const size_t nslots = epilogue == kEpiPieces ? (size_t)p.G + p.tiles : (size_t)2 * p.G;
+  return (with_counters ? counters_elems(p) : 0) + nslots * kRows * np;
+}
+
+bool gemv_pieces_plan(int dtype, int M, int N, int K, Pieces* out) {
+  if (!gemv_tc_applicable(dtype, M, N, K)) return false;
+  const Part p = make_part(N, K, kEpiPieces);
+  out->slots = nullptr;
+  out->total = p.total;
+  out->G = p.G;
+  out->nk = p.nk;
+  out->np = M <= 16 ? 16 : 32;
+  return true;
 }
 
 size_t gemv_tc_tiles(int N, int epilogue) {
@@ -263,6 +283,7 @@ cudaError_t launch_gemv_tc(const LinearArgs& a, cudaStream_t s) {
   switch (a.epilogue) {
     case kEpiStore: return launch_np<kEpiStore>(a, s);
     case kEpiResid: return launch_np<kEpiResid>(a, s);
+    case kEpiPieces: return launch_np<kEpiPieces>(a, s);
     default: return launch_np<kEpiSwiGLU>(a, s);
   }
 }

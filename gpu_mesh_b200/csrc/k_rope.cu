@@ -35,9 +35,18 @@ __global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_kernel(QkvPostArgs
     pos = pos < 0 ? 0 : a.max_pos - 1;
   }
 
-  const T* src = (const T*)a.qkv + (size_t)m * nh * D + (size_t)hh * D;
   float* x = xs[warp];
-  for (int d = lane; d < D; d += 32) x[d] = ldf<T>(src + d);
+  if (a.use_pieces) {  // the projection's pieces, rounded as its store epilogue would
+    for (int d = lane * 4; d < D; d += 128) {
+      float acc[4];
+      pieces_sum4(a.pieces, m, hh * D + d, acc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[d + i] = rt<T>(acc[i]);
+    }
+  } else {
+    const T* src = (const T*)a.qkv + (size_t)m * nh * D + (size_t)hh * D;
+    for (int d = lane; d < D; d += 32) x[d] = ldf<T>(src + d);
+  }
   __syncwarp();
 
   const bool is_q = hh < a.nq;

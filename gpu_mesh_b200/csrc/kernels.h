@@ -62,7 +62,84 @@ enum Epilogue : int {
   kEpiStore = 0,   // Y = round(acc)
   kEpiResid = 1,   // Y = round(R + round(acc))            (o_proj / down_proj + residual)
   kEpiSwiGLU = 2,  // Y[:, n] = round(round(silu(round(acc_gate))) * round(acc_up))
+  kEpiPieces = 3,  // decode GEMM only: every CTA's fp32 sums left as pieces (see Pieces)
 };
+
+// The fp32 pieces a decode GEMM leaves with kEpiPieces: the stream-K split
+// of tiles x K blocks over G CTAs (tile t = W rows 128t .. 128t + 127), and
+// CTA c's sums for tile t at slots[((c + t) · np + m) · 128 + r] for token m,
+// row r.  The kernel that consumes the output adds the pieces of a tile in
+// CTA order, which is the order the GEMM's own fix-up uses, so the results
+// are the same bits.
+struct Pieces {
+  const float* slots;
+  long long total;  // tiles · nk units
+  int G, nk, np;
+};
+
+__host__ __device__ inline void pieces_range(const Pieces& p, int t, int& c_lo, int& c_hi) {
+  c_lo = (int)((((long long)t * p.nk + 1) * p.G - 1) / p.total);
+  c_hi = (int)((((long long)(t + 1) * p.nk) * p.G - 1) / p.total);
+}
+
+#ifdef __CUDACC__
+// Sum of the pieces for token m, W rows f .. f + 7 (f a multiple of 8).
+__device__ inline void pieces_sum8(const Pieces& p, int m, int f, float* out) {
+  const int t = f >> 7, r = f & 127;
+  int c_lo, c_hi;
+  pieces_range(p, t, c_lo, c_hi);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = 0.f;
+  for (int c0 = c_lo; c0 <= c_hi; c0 += 4) {
+    float4 buf[4][2];  // four pieces' loads in flight, added in order below
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (c0 + k > c_hi) break;
+      const float4* s = reinterpret_cast<const float4*>(p.slots + ((size_t)(c0 + k + t) * p.np + m) * 128 + r);
+      buf[k][0] = __ldcg(s);
+      buf[k][1] = __ldcg(s + 1);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (c0 + k > c_hi) break;
+      out[0] += buf[k][0].x; out[1] += buf[k][0].y; out[2] += buf[k][0].z; out[3] += buf[k][0].w;
+      out[4] += buf[k][1].x; out[5] += buf[k][1].y; out[6] += buf[k][1].z; out[7] += buf[k][1].w;
+    }
+  }
+}
+
+// Sum of the pieces for token m, W rows f .. f + 3 (f a multiple of 4).
+__device__ inline void pieces_sum4(const Pieces& p, int m, int f, float* out) {
+  const int t = f >> 7, r = f & 127;
+  int c_lo, c_hi;
+  pieces_range(p, t, c_lo, c_hi);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = 0.f;
+  for (int c0 = c_lo; c0 <= c_hi; c0 += 8) {
+    float4 buf[8];  // eight pieces' loads in flight, added in order below
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (c0 + k > c_hi) break;
+      buf[k] = __ldcg(reinterpret_cast<const float4*>(p.slots + ((size_t)(c0 + k + t) * p.np + m) * 128 + r));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (c0 + k > c_hi) break;
+      out[0] += buf[k].x; out[1] += buf[k].y; out[2] += buf[k].z; out[3] += buf[k].w;
+    }
+  }
+}
+#endif
+
+// The split a kEpiPieces decode GEMM of this shape uses (slots not set);
+// false if the shape does not run on the decode GEMM.
+bool gemv_pieces_plan(int dtype, int M, int N, int K, Pieces* out);
+
+// x[m] = round(x[m] + round(pieces[m])) for the M rows of a residual stream
+// [M, H] (the o_proj / down_proj residual epilogue), then, if w is not NULL,
+// xn[m] = RMSNorm(x[m]) · w with the reduction order of the RMSNorm kernel.
+cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const void* w, void* xn, int M,
+                                     int H, float eps, cudaStream_t s);
 
 // Attention mask policies.
 enum MaskPolicy : int {
@@ -103,6 +180,8 @@ cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t x_row_stride, const
 struct QkvPostArgs {
   int dtype;
   const void* qkv;         // [M, (nq + 2 nkv) * D]
+  int use_pieces;          // read the qkv projection as pieces (bf16 decode) instead of `qkv`
+  Pieces pieces;
   const int64_t* positions;// [M] or NULL (position = past + s)
   const RowDesc* rows;     // [B]
   const void* q_norm;      // [D] or NULL
