@@ -26,6 +26,10 @@ __global__ void embed_kernel(const T* __restrict__ table, const int64_t* __restr
   for (int i = threadIdx.x; i < H / VEC; i += blockDim.x) dst[i] = src[i];
 }
 
+// RMSNorm reduction order, shared by every kernel that normalises a row
+// (this file and the layer chain): 512 threads, thread j adds the squares of
+// the 16-byte vectors j, j + 512, ... (each vector's elements in order), then
+// a butterfly over each warp's 32 lanes, then over the 16 warp sums.
 template <typename T>
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -68,10 +72,10 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __r
 }
 
 // The residual epilogue of a decode GEMM left as pieces, then (optionally)
-// the RMSNorm of the new residual row: thread j owns 8-element vectors j,
-// j + 128, ... as in rmsnorm_kernel at 128 threads, so the sum of squares is
-// added in the same order.
-__global__ void __launch_bounds__(128) resid_norm_pieces_kernel(Pieces pc, __nv_bfloat16* __restrict__ x,
+// the RMSNorm of the new residual row, in the RMSNorm reduction order (one
+// 8-element vector per thread at H <= 4096, so every piece load of the row
+// is in flight at once).
+__global__ void __launch_bounds__(kNormThreads) resid_norm_pieces_kernel(Pieces pc, __nv_bfloat16* __restrict__ x,
                                                                 const __nv_bfloat16* __restrict__ w, int H,
                                                                 float eps, __nv_bfloat16* __restrict__ y) {
   pdl_trigger();
@@ -139,7 +143,7 @@ cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const
                                      int H, float eps, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (dtype != kBF16 || H % 8 || !pc.slots) return cudaErrorInvalidValue;
-  { const cudaError_t _le = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(128), 0, s, pc, (__nv_bfloat16*)x,
+  { const cudaError_t _le = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(kNormThreads), 0, s, pc, (__nv_bfloat16*)x,
                                         (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
@@ -147,7 +151,7 @@ cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const
 cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t xs, const void* w, int M, int H,
                            float eps, void* y, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
-  const int threads = 128;  // the layer chain's norm steps use the same order
+  const int threads = kNormThreads;
   if (dtype == kBF16)
     { const cudaError_t _le = launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(threads), 0, s, 
         (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y); if (_le != cudaSuccess) return _le; }

@@ -146,8 +146,8 @@ __global__ void __launch_bounds__(kThreadsD, 1) layer_chain_kernel(const __grid_
   uint64_t* drain = tempty + 2;        // final MMA completion
   uint32_t* tmem_holder = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_holder + 1);
-  float* red = (float*)(tmem_holder + 4);  // [4] norm partial sums
-  volatile int* gate = (volatile int*)(tmem_holder + 8);  // highest step whose barrier this CTA passed
+  float* red = (float*)(tmem_holder + 4);  // [16] norm partial sums
+  volatile int* gate = (volatile int*)(tmem_holder + 20);  // highest step whose barrier this CTA passed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -350,28 +350,34 @@ __global__ void __launch_bounds__(kThreadsD, 1) layer_chain_kernel(const __grid_
       const StepDesc d = P.st[j];  // a copy in registers
       if (d.kind == kChainNorm) {
         if (c < P.M) {
-          // RMSNorm of row c, the order of rmsnorm_kernel at 128 threads.
+          // RMSNorm of row c in the RMSNorm reduction order (512 threads): the
+          // 128 threads play virtual threads e + 128·k, k = 0..3, and thread
+          // j's warp butterfly becomes this warp's for round k.
           const bf16* xr = (const bf16*)d.nx + (size_t)c * d.nxs;
           const bf16* w = (const bf16*)d.nw;
           bf16* yr = (bf16*)d.ny + (size_t)c * d.H;
-          float ss = 0.f;
+          const int ew = e >> 5;  // 0..3
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float ss = 0.f;
+            for (int i = e + 128 * k; i < d.H / 8; i += kNormThreads) {
+              float v[8];
+              load16_f<bf16>(xr + i * 8, v);
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) ss += v[jj] * v[jj];
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) red[ew + 4 * k] = ss;
+          }
+          epi_bar();
+          float tot = lane < 16 ? red[lane] : 0.f;
+          tot = warp_sum(tot);
+          epi_bar();
           const float4* w4 = reinterpret_cast<const float4*>(w);
-          float4 wv[4];  // the weights of this thread's (first four) vectors, loaded early
+          float4 wv[4];  // the weights of this thread's (first four) vectors
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             if (e + k * 128 < d.H / 8) wv[k] = __ldg(w4 + e + k * 128);
-          for (int i = e; i < d.H / 8; i += 128) {
-            float v[8];
-            load16_f<bf16>(xr + i * 8, v);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
-          }
-          ss = warp_sum(ss);
-          if (lane == 0) red[q] = ss;
-          epi_bar();
-          float tot = lane < 4 ? red[lane] : 0.f;
-          tot = warp_sum(tot);
-          epi_bar();
           const float rs = 1.0f / sqrtf(tot / (float)d.H + d.eps);
           for (int i = e, k4 = 0; i < d.H / 8; i += 128, ++k4) {
             float v[8], g[8];

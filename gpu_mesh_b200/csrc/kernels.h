@@ -57,6 +57,10 @@ __host__ __device__ inline size_t kv_offset_elems(int layer, int kv, int slot_ro
   return ((((size_t)(layer * 2 + kv) * slot_rows + row) * nkv + head) * cap + pos) * D;
 }
 
+// Threads of a row in the RMSNorm kernels; their reduction order is part of
+// the result (see block_sum in k_elementwise.cu).
+constexpr int kNormThreads = 512;
+
 // Linear epilogues: Y = f(X · Wᵀ).
 enum Epilogue : int {
   kEpiStore = 0,   // Y = round(acc)
