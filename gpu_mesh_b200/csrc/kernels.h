@@ -225,6 +225,10 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 // `out` itself (no combine launch); its fp32 scratch need is
 // attention_tc_scratch_elems, its counters one per (token, KV head).
 bool attention_tc_applicable(int dtype, int D, int G);
+// Prefill / multi-token attention with query tiles (k_attention_prefill.cu):
+// bf16, head_dim 64 or 128, G dividing 16, S >= 8 query tokens per row.
+bool attention_prefill_applicable(int dtype, int D, int G, int S);
+cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t s);
 size_t attention_tc_scratch_elems(int nq, int D);
 cudaError_t launch_attention_tc(const AttnArgs& a, int splits, cudaStream_t s);
 
