@@ -87,5 +87,13 @@ __device__ __forceinline__ void mma16816_full(float* d, uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Transpose of an 8x8 matrix of 16-bit values held one bf16 pair per thread
+// (row lane / 4, columns 2 (lane % 4), + 1).
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 }  // namespace attn
 }  // namespace mg

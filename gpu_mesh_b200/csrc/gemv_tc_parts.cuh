@@ -23,7 +23,7 @@ struct DLayout {
   static constexpr int kX = NP * kKB * 2;
   static constexpr int kStage = kWBytes + kX;  // a multiple of 1024
   static constexpr int kTiles = kStagesD * kStage;
-  static constexpr int kXchg = 64 * NP * 4;
+  static constexpr int kXchg = 64 * (NP + 1) * 4;  // padded rows: no bank conflicts
   static constexpr int kBarOff = kTiles + kXchg;
   static constexpr int kBytes = kBarOff + 1024 + 512;
 };
@@ -88,7 +88,7 @@ __device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const f
     if (r >= 64) {
 #pragma unroll
       for (int i = 0; i < NP; ++i)
-        if (i >= m_lo && i < m_hi) xchg[(r - 64) * NP + i] = v[i];
+        if (i >= m_lo && i < m_hi) xchg[(r - 64) * (NP + 1) + i] = v[i];
     }
     epi_bar();
     if (r < 64) {
@@ -98,7 +98,7 @@ __device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const f
 #pragma unroll
         for (int tok = 0; tok < NP; ++tok) {
           if (tok < m_lo || tok >= m_hi) continue;
-          const float g = rt<bf16>(v[tok]), u = rt<bf16>(xchg[r * NP + tok]);
+          const float g = rt<bf16>(v[tok]), u = rt<bf16>(xchg[r * (NP + 1) + tok]);
           const float sg = rt<bf16>(g / (1.0f + expf(-g)));
           Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(sg * u);
         }

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
   using L = TcAttnLayout<D>;
   constexpr int DB = L::kDB;
   constexpr int KS = D / 16;  // k-steps of the score MMA
-  constexpr int DN = D / 8;   // dim n-tiles of the output
+  constexpr int DM = D / 16;  // dim tiles of Oᵀ
   const int G = a.nq / a.nkv;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -244,113 +244,108 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
       const int kb = (int)(u - p * C), ke = (int)(pe - p * C);
       const int kl = min(ke, (nvis + kChunk - 1) / kChunk);  // chunks [kb, kl) hold visible keys
 
-      float mrow = -INFINITY, lrow = 0.f;
-      float o[DN][4];
+      // Transposed products, so the G <= 8 query heads sit on the MMA's N = 8
+      // side instead of padding its M = 16: Sᵀ = K·Qᵀ (M = this warp's 16
+      // keys, N = heads, K = dims) and Oᵀ = Vᵀ·Pᵀ (M = 16 dims per tile,
+      // N = heads, K = the 16 keys).  A thread holds keys g, g + 8 (dims g,
+      // g + 8 of Oᵀ) for heads 2t and 2t + 1.
+      float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+      float o[DM][4];
 #pragma unroll
-      for (int i = 0; i < DN; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      uint32_t qa[KS][2];
+      for (int i = 0; i < DM; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      uint32_t qb[KS][2];  // B fragments of Qᵀ
       for (int kc = kb; kc < kl; ++kc) {
         const int s = (int)(n % stages);
         if (!mbar_wait(&full[s], (int)(n / stages) & 1, a.err)) *abort_flag = 1;
         ++n;
         if (*abort_flag) break;  // the vote at the end of the piece stops every warp
         uint8_t* st = smem + s * L::kStage;
-        uint8_t* Vc = st + L::kKV;
         if (kc == kb) {
           const __nv_bfloat16* Qs = (const __nv_bfloat16*)(st + 2 * L::kKV);
 #pragma unroll
           for (int ks = 0; ks < KS; ++ks) {
             if (g < G) {
-              qa[ks][0] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 2 * t);
-              qa[ks][1] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 8 + 2 * t);
+              qb[ks][0] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 2 * t);
+              qb[ks][1] = *reinterpret_cast<const uint32_t*>(Qs + g * D + 16 * ks + 8 + 2 * t);
             } else {
-              qa[ks][0] = qa[ks][1] = 0u;
+              qb[ks][0] = qb[ks][1] = 0u;
             }
           }
         }
         const int nk = max(0, min(kKeysW, nvis - (kc * kChunk + warp * kKeysW)));
         if (nk > 0) {
-          // Scores for 16 keys = 2 n-tiles of 8.
-          float sc[2][4];
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+          float sc[4] = {0.f, 0.f, 0.f, 0.f};  // Sᵀ: keys g, g + 8 x heads 2t, 2t + 1
           const uint32_t kbase = smem_u32(st);
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-            for (int ks = 0; ks < KS; ks += 2) {
-              // four 8x8 matrices: keys 8nt..8nt+7 of this warp, dim chunks 2ks .. 2ks+3
-              const int r = warp * kKeysW + 8 * nt + (lane & 7);
-              const int cc = 2 * ks + (lane >> 3);
-              uint32_t bfr[4];
-              ldsm_x4(kbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), bfr);
-              mma16816(sc[nt], qa[ks][0], qa[ks][1], bfr[0], bfr[1]);
-              mma16816(sc[nt], qa[ks + 1][0], qa[ks + 1][1], bfr[2], bfr[3]);
-            }
+          for (int ks = 0; ks < KS; ++ks) {
+            // A = keys x 16 dims: four 8x8 matrices (keys 0-7 / 8-15, dim chunks 2ks / 2ks + 1)
+            const int r = warp * kKeysW + (lane & 7) + 8 * ((lane >> 3) & 1);
+            const int cc = 2 * ks + (lane >> 4);
+            uint32_t afr[4];
+            ldsm_x4(kbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), afr);
+            mma16816_full(sc, afr[0], afr[1], afr[2], afr[3], qb[ks][0], qb[ks][1]);
           }
-          // Online softmax of head g (columns 2t, 2t+1 of each n-tile).
-          float mx = mrow;
+          // Online softmax per head (column): keys g (c0, c1) and g + 8 (c2, c3).
+          const bool vA = g < nk, vB = g + 8 < nk;
+          float s0 = vA ? sc[0] * scale2 : -INFINITY, s1 = vA ? sc[1] * scale2 : -INFINITY;
+          float s2 = vB ? sc[2] * scale2 : -INFINITY, s3 = vB ? sc[3] * scale2 : -INFINITY;
+          float mx0 = fmaxf(mrow[0], fmaxf(s0, s2)), mx1 = fmaxf(mrow[1], fmaxf(s1, s3));
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int key = 8 * nt + 2 * t + e;
-              const float v = key < nk ? sc[nt][e] * scale2 : -INFINITY;
-              sc[nt][e] = v;
-              mx = fmaxf(mx, v);
-            }
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float keep = mrow == -INFINITY ? 0.f : exp2f(mrow - mx);
-          float sum = 0.f;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float pv = sc[nt][e] == -INFINITY ? 0.f : exp2f(sc[nt][e] - mx);
-              sc[nt][e] = pv;
-              sum += pv;
-            }
-          sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-          sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-          mrow = mx;
-          lrow = lrow * keep + sum;
-#pragma unroll
-          for (int i = 0; i < DN; ++i) {
-            o[i][0] *= keep;
-            o[i][1] *= keep;
+          for (int off = 4; off < 32; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
           }
-          if (nk < kKeysW) {
-            // Rows past the visible keys hold whatever the cache held (or the
-            // next head's values): P is 0 there, but 0 * NaN is not, so clear them.
-            const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-            for (int i = lane; i < (kKeysW - nk) * DB * 8; i += 32) {
-              const int rr = warp * kKeysW + nk + i / (DB * 8), rem = i % (DB * 8);
-              *reinterpret_cast<uint4*>(Vc + (rem >> 3) * kBoxBytes + rr * 128 + (rem & 7) * 16) = zero;
-            }
-            // The stage is refilled by TMA later: order these writes before it.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-          }
-          // O += P·V over one k-tile of 16 keys.  P = hi + lo, both bf16: two
-          // MMAs keep P to ~2^-17 relative, so the product matches an fp32 P·V.
-          const uint32_t vbase = smem_u32(Vc);
-          const uint32_t pa0 = pack2(sc[0][0], sc[0][1]);
-          const uint32_t pa2 = pack2(sc[1][0], sc[1][1]);
-          const uint32_t pl0 = pack2(sc[0][0] - lo_bf16(pa0), sc[0][1] - hi_bf16(pa0));
-          const uint32_t pl2 = pack2(sc[1][0] - lo_bf16(pa2), sc[1][1] - hi_bf16(pa2));
+          const float keep0 = mrow[0] == -INFINITY ? 0.f : exp2f(mrow[0] - mx0);
+          const float keep1 = mrow[1] == -INFINITY ? 0.f : exp2f(mrow[1] - mx1);
+          s0 = s0 == -INFINITY ? 0.f : exp2f(s0 - mx0);
+          s1 = s1 == -INFINITY ? 0.f : exp2f(s1 - mx1);
+          s2 = s2 == -INFINITY ? 0.f : exp2f(s2 - mx0);
+          s3 = s3 == -INFINITY ? 0.f : exp2f(s3 - mx1);
+          float sum0 = s0 + s2, sum1 = s1 + s3;
 #pragma unroll
-          for (int dn = 0; dn < DN; dn += 2) {
-            // matrices: keys +0..7 / +8..15 of this warp, dim chunks dn / dn+1
+          for (int off = 4; off < 32; off <<= 1) {
+            sum0 += __shfl_xor_sync(0xffffffffu, sum0, off);
+            sum1 += __shfl_xor_sync(0xffffffffu, sum1, off);
+          }
+          mrow[0] = mx0;
+          mrow[1] = mx1;
+          lrow[0] = lrow[0] * keep0 + sum0;
+          lrow[1] = lrow[1] * keep1 + sum1;
+#pragma unroll
+          for (int i = 0; i < DM; ++i) {
+            o[i][0] *= keep0;
+            o[i][1] *= keep1;
+            o[i][2] *= keep0;
+            o[i][3] *= keep1;
+          }
+          // Pᵀ as the B operand of Oᵀ += Vᵀ·Pᵀ: the accumulator pairs are an 8x8
+          // (keys x heads) matrix each, transposed in registers.  P = hi + lo,
+          // both bf16: two MMAs keep P to ~2^-17 relative (an fp32 P·V).
+          const uint32_t h01 = pack2(s0, s1), h23 = pack2(s2, s3);
+          const uint32_t l01 = pack2(s0 - lo_bf16(h01), s1 - hi_bf16(h01));
+          const uint32_t l23 = pack2(s2 - lo_bf16(h23), s3 - hi_bf16(h23));
+          const uint32_t pb0 = movm_trans(h01), pb1 = movm_trans(h23);
+          const uint32_t pc0 = movm_trans(l01), pc1 = movm_trans(l23);
+          // Value rows past the visible keys can hold anything (P is 0 there,
+          // but 0 * NaN is not): their halves of the A fragments are cleared.
+          const int kr = 2 * t;  // A fragment keys: kr, kr + 1 (a0, a1) and kr + 8, kr + 9 (a2, a3)
+          const uint32_t m01 = (kr < nk ? 0x0000ffffu : 0u) | (kr + 1 < nk ? 0xffff0000u : 0u);
+          const uint32_t m89 = (kr + 8 < nk ? 0x0000ffffu : 0u) | (kr + 9 < nk ? 0xffff0000u : 0u);
+          const uint32_t vbase = smem_u32(st + L::kKV);
+#pragma unroll
+          for (int dm = 0; dm < DM; ++dm) {
+            // A = Vᵀ (16 dims x 16 keys): matrices (keys 0-7 / 8-15) x (dim chunks 2dm / 2dm + 1)
             const int mi = lane >> 3;
-            const int r = warp * kKeysW + (lane & 7) + 8 * (mi & 1);
-            const int cc = dn + (mi >> 1);
-            uint32_t bfr[4];
-            ldsm_x4_t(vbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), bfr);
-            mma16816(o[dn], pa0, pa2, bfr[0], bfr[1]);
-            mma16816(o[dn], pl0, pl2, bfr[0], bfr[1]);
-            mma16816(o[dn + 1], pa0, pa2, bfr[2], bfr[3]);
-            mma16816(o[dn + 1], pl0, pl2, bfr[2], bfr[3]);
+            const int r = warp * kKeysW + (lane & 7) + 8 * (mi >> 1);
+            const int cc = 2 * dm + (mi & 1);
+            uint32_t afr[4];
+            ldsm_x4_t(vbase + (cc >> 3) * kBoxBytes + swz(r, cc & 7), afr);
+            afr[0] &= m01;
+            afr[1] &= m01;
+            afr[2] &= m89;
+            afr[3] &= m89;
+            mma16816_full(o[dm], afr[0], afr[1], afr[2], afr[3], pb0, pb1);
+            mma16816_full(o[dm], afr[0], afr[1], afr[2], afr[3], pc0, pc1);
           }
         }
         // The stage's data is in registers now: hand it back to the producer.
@@ -360,15 +355,19 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
 
       // End of the piece: merge the warps.
       float* mw = merge + warp * G * (D + 2);
-      if (g < G) {
-        if (t == 0) {
-          mw[g * (D + 2)] = mrow;
-          mw[g * (D + 2) + 1] = lrow;
-        }
 #pragma unroll
-        for (int dn = 0; dn < DN; ++dn) {
-          mw[g * (D + 2) + 2 + 8 * dn + 2 * t] = o[dn][0];
-          mw[g * (D + 2) + 2 + 8 * dn + 2 * t + 1] = o[dn][1];
+      for (int e = 0; e < 2; ++e) {  // heads 2t and 2t + 1
+        const int hh = 2 * t + e;
+        if (hh < G) {
+          if (g == 0) {
+            mw[hh * (D + 2)] = mrow[e];
+            mw[hh * (D + 2) + 1] = lrow[e];
+          }
+#pragma unroll
+          for (int dm = 0; dm < DM; ++dm) {
+            mw[hh * (D + 2) + 2 + 16 * dm + g] = o[dm][e];
+            mw[hh * (D + 2) + 2 + 16 * dm + g + 8] = o[dm][2 + e];
+          }
         }
       }
       if (consumer_any(*abort_flag)) {  // also orders the writes above

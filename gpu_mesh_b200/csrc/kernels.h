@@ -94,17 +94,17 @@ __device__ inline void pieces_sum8(const Pieces& p, int m, int f, float* out) {
   pieces_range(p, t, c_lo, c_hi);
 #pragma unroll
   for (int i = 0; i < 8; ++i) out[i] = 0.f;
-  for (int c0 = c_lo; c0 <= c_hi; c0 += 4) {
-    float4 buf[4][2];  // four pieces' loads in flight, added in order below
+  for (int c0 = c_lo; c0 <= c_hi; c0 += 8) {
+    float4 buf[8][2];  // eight pieces' loads in flight, added in order below
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 8; ++k) {
       if (c0 + k > c_hi) break;
       const float4* s = reinterpret_cast<const float4*>(p.slots + ((size_t)(c0 + k + t) * p.np + m) * 128 + r);
       buf[k][0] = __ldcg(s);
       buf[k][1] = __ldcg(s + 1);
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 8; ++k) {
       if (c0 + k > c_hi) break;
       out[0] += buf[k][0].x; out[1] += buf[k][0].y; out[2] += buf[k][0].z; out[3] += buf[k][0].w;
       out[4] += buf[k][1].x; out[5] += buf[k][1].y; out[6] += buf[k][1].z; out[7] += buf[k][1].w;
