@@ -412,6 +412,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=32,
                     help="decoder layers (32 = Llama-3-8B; fewer only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="N > 1: skip the weak-scaling measurement (N groups of 32 rows in flight)")
     ap.add_argument("--no-long-context", action="store_true",
                     help="skip the long-context attention measurement (64 rows x 8192 positions)")
     args = ap.parse_args()

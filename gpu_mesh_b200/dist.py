@@ -219,6 +219,54 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
         stage.profile(False)
         ids, e2e_ms = timed(lambda: run(args.steps, ids, forward_decode, sample_host, hid_decode))
 
+        # Weak scaling: the same per-GPU work at a batch that grows with N
+        # (N groups of 32 rows in flight: every GPU streams its weights N
+        # times per step, as one GPU streams all weights once for 32 rows).
+        weak = None
+        if world > 1 and not getattr(args, "no_weak", False):
+            for sl in slots:
+                stage.kv_free(sl)
+            torch.cuda.empty_cache()
+            rows_w = rows_total
+            slots_w = list(range(101, 101 + n_groups))
+            for sl in slots_w:
+                stage.kv_reserve(sl, rows_w, cap)
+            gw = torch.Generator().manual_seed(2000)
+            prompts_w = [torch.randint(0, cfg.vocab_size, (rows_w, args.prompt), generator=gw).to(dev)
+                         for _ in range(n_groups)]
+            hid_pw = [torch.empty(rows_w, args.prompt, H, dtype=torch.bfloat16, device=dev)
+                      for _ in range(n_groups)]
+            hid_dw = [torch.empty(rows_w, 1, H, dtype=torch.bfloat16, device=dev) for _ in range(n_groups)]
+            ids_w = [torch.empty(rows_w, 1, dtype=torch.int64, device=dev) for _ in range(n_groups)]
+
+            def fwd_pw(k, grp, x):
+                if ring.first:
+                    return stage.forward_slot(slots_w[grp], None, input_ids=x, logits="last", check_values=False)
+                return stage.forward_slot(slots_w[grp], x, logits="last", check_values=False)
+
+            def fwd_dw(k, grp, x):
+                if ring.first:
+                    return stage.decode_multi([slots_w[grp]], None, input_ids=x, logits="last")
+                return stage.decode_multi([slots_w[grp]], x, logits="last")
+
+            def run_w(n_steps, inputs, fwd, hid):
+                return decode_loop(ring, n_groups, n_steps, inputs, fwd, sample,
+                                   lambda k, grp: hid[grp], lambda grp: ids_w[grp], ret_group=ret_group)
+
+            idw, _ = timed(lambda: run_w(1, prompts_w, fwd_pw, hid_pw))
+            idw, _ = timed(lambda: run_w(args.warmup, idw, fwd_dw, hid_dw))
+            idw, ms_w = timed(lambda: run_w(args.steps, idw, fwd_dw, hid_dw))
+            weak = {
+                "scaling": "weak",
+                "rows": rows_w * n_groups,
+                "groups_in_flight": n_groups,
+                "rows_per_group": rows_w,
+                "value": rows_w * n_groups * args.steps / (ms_w / 1000.0),
+                "unit": "tok/s",
+                "ms_per_step": ms_w / args.steps,
+                "note": "per-GPU work of the one-GPU workload (32 rows through every layer once per step)",
+            }
+
         profs = [None] * world
         dist.all_gather_object(profs, prof)
         counts = [0] * world
@@ -279,6 +327,8 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 "per_stage_profile": profs,
                 "clocks": clocks.summary(),
             }
+            if weak is not None:
+                line["weak_scaling"] = weak
             print(json.dumps(line), flush=True)
         stage.close()
     finally:
