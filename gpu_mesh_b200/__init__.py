@@ -4,6 +4,7 @@ Dense decoder stages (Llama and Qwen3 architectures) run on hand-written
 sm_100a CUDA kernels behind a C ABI (``include/meshgpu_b200.h``); this package
 is the Python host side with the reference's stage / pipeline API.
 """
+from gpu_mesh_b200.batcher import ContinuousBatcher, SessionResult
 from gpu_mesh_b200.config import LlamaConfig, config_from, split_layers
 from gpu_mesh_b200.pipeline import (
     build_pipeline,
@@ -20,9 +21,11 @@ from gpu_mesh_b200.stage_worker import B200StageWorker, ForwardResult, StageCont
 __all__ = [
     "B200Stage",
     "B200StageWorker",
+    "ContinuousBatcher",
     "ForwardResult",
     "LlamaConfig",
     "SamplingParams",
+    "SessionResult",
     "StageContext",
     "build_pipeline",
     "config_from",
