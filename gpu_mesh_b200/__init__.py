@@ -6,6 +6,7 @@ is the Python host side with the reference's stage / pipeline API.
 """
 from gpu_mesh_b200.batcher import ContinuousBatcher, SessionResult
 from gpu_mesh_b200.config import LlamaConfig, config_from, split_layers
+from gpu_mesh_b200.manifest import ModelManifest, build_pipeline_from_manifest, build_stage_from_manifest
 from gpu_mesh_b200.pipeline import (
     build_pipeline,
     from_reference_workers,
@@ -24,10 +25,13 @@ __all__ = [
     "ContinuousBatcher",
     "ForwardResult",
     "LlamaConfig",
+    "ModelManifest",
     "SamplingParams",
     "SessionResult",
     "StageContext",
     "build_pipeline",
+    "build_pipeline_from_manifest",
+    "build_stage_from_manifest",
     "config_from",
     "from_reference_workers",
     "greedy_sample",
