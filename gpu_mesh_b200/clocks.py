@@ -1,13 +1,19 @@
 """GPU clock and throttle-reason sampling during a timed region.
 
-``nvidia-smi`` is polled every 200 ms in a child process while the region
-runs; the summary (median SM clock under load, max clock, active throttle
-reasons) goes into the benchmark's JSON line so a throttled or clock-locked
-run can be recognised.  Reading clocks changes no GPU setting.
+``nvidia-smi`` polls the GPU in a child process; a reader thread stamps each
+line with the host clock.  Entering the context waits (up to a few seconds)
+for the first sample, so the poller is running before the timed region
+starts, and leaving it waits for one more sample, so a region shorter than
+the polling interval still has one.  The summary keeps only samples stamped
+inside the region (or the first one after it ends when none is): median SM
+clock under load, max clock, active throttle reasons.  Reading clocks
+changes no GPU setting.
 """
 from __future__ import annotations
 
 import subprocess
+import threading
+import time
 
 
 class ClockSampler:
@@ -16,37 +22,70 @@ class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
+    START_WAIT_S = 5.0
 
     def __init__(self, gpu: int) -> None:
         self.gpu = gpu
         self.proc = None
+        self.samples: list[tuple[float, str]] = []
+        self.t0 = self.t1 = 0.0
+        self._cv = threading.Condition()
+        self._reader = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            if line.strip():
+                with self._cv:
+                    self.samples.append((time.monotonic(), line))
+                    self._cv.notify_all()
+
+    def _wait_for(self, count: int, timeout: float) -> None:
+        with self._cv:
+            self._cv.wait_for(lambda: len(self.samples) >= count, timeout=timeout)
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"],
+                 "-lms", str(self.INTERVAL_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
             )
         except (FileNotFoundError, OSError):
             self.proc = None
+        if self.proc is not None:
+            self._reader = threading.Thread(target=self._read, daemon=True)
+            self._reader.start()
+            self._wait_for(1, self.START_WAIT_S)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        self.t1 = time.monotonic()
+        if self.proc is None:
+            return
+        with self._cv:
+            after = len(self.samples) + 1
+        self._wait_for(after, 1.0)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+        if self._reader is not None:
+            self._reader.join(timeout=5)
+
+    def region_lines(self) -> list[str]:
+        inside = [line for t, line in self.samples if self.t0 <= t <= self.t1]
+        if not inside:
+            inside = [line for t, line in self.samples if t > self.t1][:1]
+        return inside
 
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
+        for line in self.region_lines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
