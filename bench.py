@@ -237,7 +237,7 @@ def long_context(hbm: float, *, rows: int = 64, context: int = 8192, layers: int
 
 def run_single(args) -> None:
     from gpu_mesh_b200 import _lib, build_pipeline, greedy_sample
-    from gpu_mesh_b200.pipeline import pipeline_decode_multi
+    from gpu_mesh_b200.pipeline import pipeline_decode_greedy
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -269,8 +269,8 @@ def run_single(args) -> None:
     ids = torch.cat(first).unsqueeze(-1)
 
     def step(ids):
-        logits = w.decode_multi(None, keys, input_ids=ids, logits="last")
-        return greedy_sample(logits[:, -1]).unsqueeze(-1)
+        tokens, _ = w.decode_greedy(None, keys, input_ids=ids)  # selection fused into lm_head
+        return tokens.unsqueeze(-1)
 
     for _ in range(args.warmup):
         ids = step(ids)
@@ -306,8 +306,8 @@ def run_single(args) -> None:
     e2.record()
     for _ in range(args.steps):
         d_ids = host_ids.to(dev, non_blocking=True)
-        logits = pipeline_decode_multi(workers, d_ids, cache_keys=keys, logits="last")
-        tok = greedy_sample(logits[:, -1]).unsqueeze(-1)
+        tok, _ = pipeline_decode_greedy(workers, d_ids, cache_keys=keys)
+        tok = tok.unsqueeze(-1)
         host_out.copy_(tok, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         host_ids.copy_(host_out)

@@ -127,6 +127,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mg_kv_export": (ctypes.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "mg_stage_forward": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp]),
     "mg_stage_decode_multi": (ctypes.c_int, [_vp, _i32p, _i32, _vp, _vp, _i32, _vp, _vp]),
+    "mg_stage_decode_greedy": (ctypes.c_int, [_vp, _i32p, _i32, _vp, _vp, _vp, _vp, _vp]),
     "mg_stage_check_device": (ctypes.c_int, [_vp, _vp]),
     "mg_stage_profile": (ctypes.c_int, [_vp, _i32]),
     "mg_stage_profile_read": (ctypes.c_int, [_vp, ctypes.POINTER(Profile)]),

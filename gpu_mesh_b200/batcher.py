@@ -30,7 +30,12 @@ from typing import Any
 
 import torch
 
-from gpu_mesh_b200.pipeline import pipeline_decode_multi, pipeline_decode_step, pipeline_prefill
+from gpu_mesh_b200.pipeline import (
+    pipeline_decode_greedy,
+    pipeline_decode_multi,
+    pipeline_decode_step,
+    pipeline_prefill,
+)
 from gpu_mesh_b200.sampling import SamplingParams, greedy_sample, make_sampling_generator, top_p_sample
 
 log = logging.getLogger(__name__)
@@ -329,9 +334,16 @@ class ContinuousBatcher:
             return [None] * len(batch)
         try:
             ids = torch.tensor([[s.last_token()] for s in live], dtype=torch.long)
-            logits = pipeline_decode_multi(self._workers, ids, cache_keys=[s.cache_key for s in live])
-            self.decode_passes += 1
+            keys = [s.cache_key for s in live]
             greedy = [i for i, s in enumerate(live) if s.sampling.temperature == 0.0]
+            if len(greedy) == len(live) and hasattr(self._workers[-1], "decode_greedy"):
+                # every row greedy: the last stage selects on the device, no logits leave it
+                chosen, _ = pipeline_decode_greedy(self._workers, ids, cache_keys=keys)
+                self.decode_passes += 1
+                out = {id(s): self._advance(s, int(t)) for s, t in zip(live, chosen.tolist())}
+                return [out.get(id(s)) for s in batch]
+            logits = pipeline_decode_multi(self._workers, ids, cache_keys=keys)
+            self.decode_passes += 1
             tokens: dict[int, int] = {}
             if greedy:
                 sel = torch.tensor(greedy, device=logits.device)

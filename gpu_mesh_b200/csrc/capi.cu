@@ -77,7 +77,7 @@ struct Slot {
   int batch = 0, cap = 0, len = 0;
   void* kv = nullptr;
   size_t bytes = 0;
-  void* tmap = nullptr;  // device copy of the KV tensor map (bf16, D 64/128), or NULL
+  void* tmap = nullptr;  // device copies of the two KV tensor maps (bf16, D 64/128), or NULL
 };
 
 struct ProfRec {
@@ -119,6 +119,13 @@ struct mg_stage {
   int* chain_bar = nullptr;  // layer-chain grid barrier: arrivals so far (wrapping)
   int chain_gen = 0;         // the value the device word holds between launches
   bool chain_enabled = false; // MESHGPU_LAYER_CHAIN=1 turns the decode layer chain on
+  // Greedy selection fused into lm_head (Greedy): zero between launches.
+  unsigned long long* greedy_best = nullptr;
+  int* greedy_done = nullptr;
+  // Logits of a greedy decode whose caller wants only token ids, when the
+  // selection cannot be fused (kept between calls, grown on demand).
+  void* greedy_logits = nullptr;
+  size_t greedy_logits_bytes = 0;
   void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
   float* part = nullptr;
   RowDesc* rows = nullptr;
@@ -240,6 +247,7 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   n_counters = std::max(n_counters, (size_t)Mt * st->nkv);  // attention: one per (token, KV head)
   const size_t o_counters = take(n_counters * sizeof(int));
   const size_t o_bar = take(64 * sizeof(int));  // two words, 128 bytes apart
+  const size_t o_greedy = take(64 * sizeof(unsigned long long));  // best[32], done
   if (st->work) {
     MG_CUDA(cudaDeviceSynchronize(), "synchronize before work resize");
     cudaFree(st->work);
@@ -268,6 +276,9 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   st->chain_bar = (int*)(base + o_bar);
   st->chain_gen = 0;
   MG_CUDA(cudaMemset(st->chain_bar, 0, 64 * sizeof(int)), "zero chain barrier");
+  st->greedy_best = (unsigned long long*)(base + o_greedy);
+  st->greedy_done = (int*)(st->greedy_best + 32);
+  MG_CUDA(cudaMemset(st->greedy_best, 0, 64 * sizeof(unsigned long long)), "zero greedy selection");
   st->work_bytes = off;
   st->work_tokens = Mt;
   st->work_rows = Rt;
@@ -314,14 +325,17 @@ int reserve_slot(mg_stage* st, int id, int batch, int need, cudaStream_t s) {
   sl.cap = cap;
   sl.bytes = bytes;
   st->kv_bytes += bytes;
-  // Tensor map of the block for the tensor-core attention: a 2-D bf16 view
-  // [layers*2*rows*nkv*cap, D], box kKvBoxKeys keys x 64 dims.
+  // Tensor maps of the block for the tensor-core attention: a 2-D bf16 view
+  // [layers*2*rows*nkv*cap, D], one with a box of kKvBoxKeys keys x 64 dims
+  // and, right after it, one with a box of kKvTailKeys keys for the partly
+  // visible last chunk of a sequence.
   if (attention_tc_applicable(st->cfg.dtype, st->D, st->nq / st->nkv)) {
-    CUtensorMap tm;
+    CUtensorMap tm[2];
     const uint64_t rows = (uint64_t)st->L * 2 * sl.batch * st->nkv * cap;
-    if (rows < (1ull << 31) && tc_host::make_map(&tm, kv, rows, st->D, st->D, kKvBoxKeys)) {
-      if (!sl.tmap) MG_CUDA(cudaMalloc(&sl.tmap, sizeof(CUtensorMap)), "KV tensor map");
-      MG_CUDA(cudaMemcpy(sl.tmap, &tm, sizeof(CUtensorMap), cudaMemcpyHostToDevice), "KV tensor map upload");
+    if (rows < (1ull << 31) && tc_host::make_map(&tm[0], kv, rows, st->D, st->D, kKvBoxKeys) &&
+        tc_host::make_map(&tm[1], kv, rows, st->D, st->D, kKvTailKeys)) {
+      if (!sl.tmap) MG_CUDA(cudaMalloc(&sl.tmap, sizeof(tm)), "KV tensor map");
+      MG_CUDA(cudaMemcpy(sl.tmap, tm, sizeof(tm), cudaMemcpyHostToDevice), "KV tensor map upload");
     } else if (sl.tmap) {
       cudaFree(sl.tmap);
       sl.tmap = nullptr;
@@ -420,9 +434,12 @@ int linear_class(const LinearArgs& a) {
 }
 
 // The layer loop for one batch of rows sharing the query length S.
+// `greedy_ids` (device int64 [rows of logits], last stage only): also select
+// each row's greedy token, fused into lm_head where the decode GEMM runs it;
+// `out` may then be NULL when the logits themselves are not wanted.
 int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64_t* ids,
               const void* hidden_in, const int64_t* positions, int out_mode, void* out,
-              cudaStream_t s) {
+              cudaStream_t s, int64_t* greedy_ids = nullptr) {
   const mg_stage_config& c = st->cfg;
   const int B = (int)rows.size();
   const int M = B * S;
@@ -504,6 +521,23 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   // launches as one layer-chain launch; the rest runs kernel by kernel.
   const bool last_only = out_mode == MG_OUT_LOGITS_LAST;
   const int rows_out = last_only ? B : M;
+  const bool fuse_greedy = greedy_ids && c.has_lm_head && !st->chain_enabled &&
+                           gemv_tc_applicable(dt, rows_out, st->V, H);
+  if (greedy_ids && c.has_lm_head && !out && !fuse_greedy) {
+    // the selection reads the logits: give them somewhere to go
+    const size_t need = (size_t)rows_out * st->V * st->esz;
+    if (need > st->greedy_logits_bytes) {
+      if (st->greedy_logits) {
+        MG_CUDA(cudaStreamSynchronize(s), "synchronize before logits buffer resize");
+        cudaFree(st->greedy_logits);
+        st->greedy_logits = nullptr;
+        st->greedy_logits_bytes = 0;
+      }
+      MG_CUDA(cudaMalloc(&st->greedy_logits, need), "greedy logits buffer");
+      st->greedy_logits_bytes = need;
+    }
+    out = st->greedy_logits;
+  }
   ChainArgs ca{};
   ca.dtype = dt;
   ca.M = M;
@@ -666,12 +700,16 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
                "final norm");
     la.M = rows_out;
     la.X = st->xn; la.ldx = H; la.W = st->lm_head; la.Y = out; la.ldy = st->V;
-    la.N = st->V; la.K = H; la.epilogue = kEpiStore; la.R = nullptr;
+    la.N = st->V; la.K = H; la.epilogue = fuse_greedy ? kEpiGreedy : kEpiStore; la.R = nullptr;
+    if (fuse_greedy) la.greedy = Greedy{st->greedy_best, st->greedy_done, greedy_ids};
     MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "lm_head");
   } else {
     MG_CUDA(cudaMemcpyAsync(out, st->x, (size_t)M * H * st->esz, cudaMemcpyDeviceToDevice, s),
             "hidden output copy");
   }
+  if (greedy_ids && c.has_lm_head && !fuse_greedy)
+    MG_TIMED(MG_PROF_OTHER, (double)rows_out * st->V * st->esz, 0,
+             launch_argmax(dt, out, rows_out, st->V, st->V, greedy_ids, s), "greedy selection");
   return MG_OK;
 }
 
@@ -849,6 +887,7 @@ int mg_stage_destroy(mg_stage* st) {
     if (kv.second.tmap) cudaFree(kv.second.tmap);
   }
   if (st->work) cudaFree(st->work);
+  if (st->greedy_logits) cudaFree(st->greedy_logits);
   if (st->wbuf) cudaFree(st->wbuf);
   if (st->err) cudaFree(st->err);
   if (st->ring.host) cudaFreeHost(st->ring.host);
@@ -998,9 +1037,10 @@ int mg_stage_forward(mg_stage* st, int32_t slot, const int64_t* ids, const void*
   return MG_OK;
 }
 
-int mg_stage_decode_multi(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
-                          const void* hidden_in, int32_t out_mode, void* out, void* stream) {
-  if (!st || !slots || n_slots < 1 || !out) return fail(MG_EINVAL, "null or empty argument");
+namespace {
+
+int decode_slots(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
+                 const void* hidden_in, int32_t out_mode, void* out, int64_t* greedy_ids, void* stream) {
   int rc = check_inputs(st, ids, hidden_in);
   if (rc) return rc;
   rc = check_out_mode(st, out_mode);
@@ -1027,10 +1067,25 @@ int mg_stage_decode_multi(mg_stage* st, const int32_t* slots, int32_t n_slots, c
     for (int b = 0; b < sl.batch; ++b)
       rows.push_back(RowDesc{(uint64_t)sl.kv, (uint64_t)sl.tmap, sl.batch, b, sl.cap, sl.len});
   }
-  rc = run_stage(st, rows, 1, ids, hidden_in, nullptr, out_mode, out, s);
+  rc = run_stage(st, rows, 1, ids, hidden_in, nullptr, out_mode, out, s, greedy_ids);
   if (rc) return rc;
   for (int i = 0; i < n_slots; ++i) st->slots[slots[i]].len += 1;
   return MG_OK;
+}
+
+}  // namespace
+
+int mg_stage_decode_multi(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
+                          const void* hidden_in, int32_t out_mode, void* out, void* stream) {
+  if (!st || !slots || n_slots < 1 || !out) return fail(MG_EINVAL, "null or empty argument");
+  return decode_slots(st, slots, n_slots, ids, hidden_in, out_mode, out, nullptr, stream);
+}
+
+int mg_stage_decode_greedy(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
+                           const void* hidden_in, int64_t* ids_out, void* logits_out, void* stream) {
+  if (!st || !slots || n_slots < 1 || !ids_out) return fail(MG_EINVAL, "null or empty argument");
+  if (!st->cfg.has_lm_head) return fail(MG_EINVAL, "greedy selection needs the last stage (lm_head)");
+  return decode_slots(st, slots, n_slots, ids, hidden_in, MG_OUT_LOGITS_ALL, logits_out, ids_out, stream);
 }
 
 int mg_stage_check_device(mg_stage* st, void* stream) {
@@ -1050,6 +1105,7 @@ int mg_stage_check_device(mg_stage* st, void* stream) {
     if (st->counters) cudaMemset(st->counters, 0, st->counters_elems * sizeof(int));
     if (st->chain_bar) cudaMemset(st->chain_bar, 0, 64 * sizeof(int));
     st->chain_gen = 0;
+    if (st->greedy_best) cudaMemset(st->greedy_best, 0, 64 * sizeof(unsigned long long));
     return fail(MG_EDEVICE, "a tensor-core kernel timed out waiting for its data; the outputs of "
                             "the forwards since the last check are invalid");
   }

@@ -14,7 +14,10 @@ using bf16 = __nv_bfloat16;
 
 constexpr int kRows = 128;
 constexpr int kKB = 64;
-constexpr int kStagesD = 8;  // 144-160 KB of weights in flight per SM
+#ifndef MG_GEMV_STAGES
+#define MG_GEMV_STAGES 8
+#endif
+constexpr int kStagesD = MG_GEMV_STAGES;  // 16 KB of weights per stage in flight per SM
 constexpr int kThreadsD = 192;
 constexpr int kWBytes = kRows * kKB * 2;
 
@@ -121,11 +124,69 @@ __device__ __forceinline__ void apply(const LinearArgs& a, int t, int r, const f
 #pragma unroll
     for (int tok = 0; tok < NP; ++tok)
       if (tok >= m_lo && tok < m_hi) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(rr[tok] + rt<bf16>(v[tok]));
-  } else {
+  } else if (EPI == kEpiStore || a.Y != nullptr) {
 #pragma unroll
     for (int tok = 0; tok < NP; ++tok)
       if (tok >= m_lo && tok < m_hi) Y[(size_t)tok * a.ldy] = __float2bfloat16_rn(v[tok]);
   }
+}
+
+// Greedy selection key of a logit: the bf16-rounded value in order-preserving
+// bits (NaN above everything, -0 as +0) over the complement of the index, so
+// the 64-bit maximum is the largest logit with the lowest index.
+__device__ __forceinline__ unsigned long long greedy_key(float v, int index) {
+  const float y = __bfloat162float(__float2bfloat16_rn(v));
+  uint32_t u = __float_as_uint(y);
+  if (y == 0.f) u = 0u;
+  const uint32_t ord = (y != y) ? 0xffffffffu : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+  return ((unsigned long long)ord << 32) | (uint32_t)(0xffffffffu - (uint32_t)index);
+}
+
+// Fold the finished logits of W row r of tile t (all tokens) into the
+// per-token maxima: a transposing butterfly leaves lane l holding the warp's
+// best key of token l (l < NP), then one atomic max per token and warp.
+template <int NP>
+__device__ __forceinline__ void greedy_fold(const LinearArgs& a, int t, int r, int lane, const float* v) {
+  const int f = t * kRows + r;
+  unsigned long long k[NP];
+#pragma unroll
+  for (int tok = 0; tok < NP; ++tok) k[tok] = (f < a.N && tok < a.M) ? greedy_key(v[tok], f) : 0ull;
+  if (NP == 16) {
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, k[j], 16);
+      k[j] = o > k[j] ? o : k[j];
+    }
+  }
+#pragma unroll
+  for (int w = NP / 2; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int j = 0; j < w; ++j) {
+      const unsigned long long send = up ? k[j] : k[j + w];
+      const unsigned long long keep = up ? k[j + w] : k[j];
+      const unsigned long long got = __shfl_xor_sync(0xffffffffu, send, w);
+      k[j] = got > keep ? got : keep;
+    }
+  }
+  const int tok = lane & (NP - 1);
+  if (lane < NP && tok < a.M && k[0] != 0ull) atomicMax(a.greedy.best + tok, k[0]);
+}
+
+// After a CTA's last tile: count it in; the last CTA of the grid turns the
+// keys into token ids and clears the buffers for the next launch.  `e` is the
+// thread's index among the 128 epilogue threads.
+__device__ __forceinline__ void greedy_finish(const LinearArgs& a, int e) {
+  __threadfence();
+  epi_bar();  // every warp's atomics precede the count
+  if (e != 0) return;
+  if (tc::atomic_add_acq_rel_gpu(a.greedy.done, 1) != (int)gridDim.x - 1) return;
+  for (int tok = 0; tok < a.M; ++tok) {
+    const unsigned long long key = __ldcg(a.greedy.best + tok);
+    a.greedy.ids[tok] = (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+    a.greedy.best[tok] = 0ull;
+  }
+  *a.greedy.done = 0;
 }
 
 // The fix-up of a split tile by the CTA that completed its count: add the

@@ -35,6 +35,10 @@
 #include "kernels.h"
 #include "tc_common.cuh"
 
+#ifndef MG_ATTN_CUT_COST
+#define MG_ATTN_CUT_COST 4  // chunks a CTA pays for merging its cut pairs
+#endif
+
 namespace mg {
 namespace {
 
@@ -191,10 +195,27 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
         uint8_t* st = smem + s * L::kStage;
         const int yk = (int)kv_row(a.layer, 0, rd.slot_rows, rd.row, a.nkv, h, rd.cap, k0);
         const int yv = (int)kv_row(a.layer, 1, rd.slot_rows, rd.row, a.nkv, h, rd.cap, k0);
-        mbar_expect_tx(&full[s], 2 * L::kKV);
-        for (int db = 0; db < DB; ++db) tma_load_2d_gmap(st + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yk);
-        for (int db = 0; db < DB; ++db)
-          tma_load_2d_gmap(st + L::kKV + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yv);
+        // A chunk that is only partly visible (the sequence's last) is loaded
+        // in slices of kKvTailKeys keys up to its last visible key, in the
+        // same layout; the consumers mask the keys past it.
+        const int nsl = (min(kChunk, nvis - k0) + kKvTailKeys - 1) / kKvTailKeys;
+        if (nsl * kKvTailKeys < kChunk) {
+          const uint64_t tail = rd.kv_tmap + sizeof(CUtensorMap);
+          constexpr int kSlice = kKvTailKeys * 128;
+          mbar_expect_tx(&full[s], 2 * DB * nsl * kSlice);
+          for (int j = 0; j < nsl; ++j)
+            for (int db = 0; db < DB; ++db) {
+              tma_load_2d_gmap(st + db * kBoxBytes + j * kSlice, tail, &full[s], db * 64, yk + j * kKvTailKeys);
+              tma_load_2d_gmap(st + L::kKV + db * kBoxBytes + j * kSlice, tail, &full[s], db * 64,
+                               yv + j * kKvTailKeys);
+            }
+        } else {
+          mbar_expect_tx(&full[s], 2 * L::kKV);
+          for (int db = 0; db < DB; ++db)
+            tma_load_2d_gmap(st + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yk);
+          for (int db = 0; db < DB; ++db)
+            tma_load_2d_gmap(st + L::kKV + db * kBoxBytes, rd.kv_tmap, &full[s], db * 64, yv);
+        }
         if (!q_done) {  // the piece's first loaded chunk carries its query rows
           const __nv_bfloat16* src = (const __nv_bfloat16*)a.q + ((size_t)m * a.nq + (size_t)h * G) * D;
           if (waited) {
@@ -527,7 +548,7 @@ cudaError_t launch_attention_tc(const AttnArgs& a, int splits, cudaStream_t s) {
     // Whole pairs when the busiest CTA then streams no more chunks than an
     // equal stream-K range plus what its cut pairs cost (about 4 chunks).
     const long long whole_span = (pairs + cap - 1) / cap * splits;
-    const long long sk_span = (pl.total + cap - 1) / cap + 4;
+    const long long sk_span = (pl.total + cap - 1) / cap + MG_ATTN_CUT_COST;
     pl.whole = whole_span <= sk_span;
     const long long units = pl.whole ? pairs : pl.total;
     pl.grid = (int)(units < cap ? units : cap);

@@ -21,7 +21,8 @@
 // issues tcgen05.mma (M=128, N=NP, K=16) into one of two TMEM accumulators;
 // warps 2-5 drain the other accumulator with tcgen05.ld (warp w reads TMEM
 // lanes 32*(w%4)..+31) and run the epilogue (store / residual / SwiGLU with
-// the reference's rounding points).  Launched with programmatic dependent
+// the reference's rounding points; for lm_head optionally the greedy
+// selection, see Greedy).  Launched with programmatic dependent
 // launch, the producer requests its first weights before waiting for the
 // previous kernel.  Every wait is bounded; on a timeout the
 // kernel records code 3 in the error word, drains what it issued, frees its
@@ -185,7 +186,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       const bool whole = lo == (long long)t * p.nk && hi == (long long)(t + 1) * p.nk;
       if (!whole && !piece_done<NP>(p, slots, counters, c, t, r, e, v)) continue;  // another CTA finishes it
       apply<NP, EPI>(a, t, r, v, xchg);
+      if (EPI == kEpiGreedy) greedy_fold<NP>(a, t, r, lane, v);
     }
+    if (EPI == kEpiGreedy && ok) greedy_finish(a, e);
     if (!ok) *abort_flag = 1;
   }
 
@@ -284,6 +287,9 @@ cudaError_t launch_gemv_tc(const LinearArgs& a, cudaStream_t s) {
     case kEpiStore: return launch_np<kEpiStore>(a, s);
     case kEpiResid: return launch_np<kEpiResid>(a, s);
     case kEpiPieces: return launch_np<kEpiPieces>(a, s);
+    case kEpiGreedy:
+      if (!a.greedy.best || !a.greedy.done || !a.greedy.ids) return cudaErrorInvalidValue;
+      return launch_np<kEpiGreedy>(a, s);
     default: return launch_np<kEpiSwiGLU>(a, s);
   }
 }

@@ -42,10 +42,14 @@ struct RowDesc {
   int32_t past;       // cached positions before this forward
 };
 
-// The KV tensor map of a slot views its block as a 2-D bf16 array
-// [layers*2*rows*nkv*cap, D] with a box of kKvBoxKeys keys x 64 dims and a
-// 128-byte swizzle; kv_row() is the row of (layer, K|V, row, head, pos).
+// The KV tensor maps of a slot view its block as a 2-D bf16 array
+// [layers*2*rows*nkv*cap, D] with a 128-byte swizzle: at kv_tmap a box of
+// kKvBoxKeys keys x 64 dims, at kv_tmap + sizeof(CUtensorMap) a box of
+// kKvTailKeys keys (the last, partly visible chunk of a sequence is loaded in
+// such slices, in the same shared-memory layout); kv_row() is the row of
+// (layer, K|V, row, head, pos).
 constexpr int kKvBoxKeys = 128;
+constexpr int kKvTailKeys = 16;
 __host__ __device__ inline int64_t kv_row(int layer, int kv, int slot_rows, int row, int nkv,
                                           int head, int cap, int pos) {
   return ((((int64_t)(layer * 2 + kv) * slot_rows + row) * nkv + head) * cap + pos);
@@ -67,6 +71,19 @@ enum Epilogue : int {
   kEpiResid = 1,   // Y = round(R + round(acc))            (o_proj / down_proj + residual)
   kEpiSwiGLU = 2,  // Y[:, n] = round(round(silu(round(acc_gate))) * round(acc_up))
   kEpiPieces = 3,  // decode GEMM only: every CTA's fp32 sums left as pieces (see Pieces)
+  kEpiGreedy = 4,  // decode GEMM only (lm_head): kEpiStore (Y may be NULL) + per-row argmax (see Greedy)
+};
+
+// Greedy selection fused into the lm_head decode GEMM.  Every CTA folds the
+// rounded logits of the tiles it finishes into best[m], one 64-bit atomic max
+// per token row and warp of a packed key (order-preserving bits of the bf16
+// logit << 32 | ~vocab index: the largest logit, then the lowest index, as
+// torch.argmax); the last CTA to finish (counted in *done) writes
+// ids[m] = the index, and returns best[] and *done to zero.
+struct Greedy {
+  unsigned long long* best;  // [32], zero between launches
+  int* done;                 // zero between launches
+  int64_t* ids;              // [M] token ids out
 };
 
 // The fp32 pieces a decode GEMM leaves with kEpiPieces: the stream-K split
@@ -168,6 +185,8 @@ struct LinearArgs {
   // front of `partial` and cleared by the launcher before every launch.
   int* counters;
   size_t counters_elems;
+  // kEpiGreedy: the selection buffers (device pointers; unused otherwise).
+  Greedy greedy{nullptr, nullptr, nullptr};
 };
 
 // Scratch (fp32 elements) that launch_linear needs for the given shape.
@@ -216,6 +235,8 @@ struct AttnArgs {
   // launch starts and zero again when it ends.
   int* counters;
   size_t counters_elems;
+  // kEpiGreedy: the selection buffers (device pointers; unused otherwise).
+  Greedy greedy{nullptr, nullptr, nullptr};
 };
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);

@@ -167,18 +167,30 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 return stage.forward_slot(slots[grp], None, input_ids=x, logits="last", check_values=False)
             return stage.forward_slot(slots[grp], x, logits="last", check_values=False)
 
-        def forward_decode(k, grp, x):
+        def decode_on(slot_ids, x):
+            # the last stage selects the greedy tokens inside its lm_head
+            if ring.last:
+                return stage.decode_greedy(slot_ids, None if ring.first else x,
+                                           input_ids=x if ring.first else None)[0]
             if ring.first:
-                return stage.decode_multi([slots[grp]], None, input_ids=x, logits="last")
-            return stage.decode_multi([slots[grp]], x, logits="last")
+                return stage.decode_multi(slot_ids, None, input_ids=x, logits="last")
+            return stage.decode_multi(slot_ids, x, logits="last")
 
-        def sample(k, grp, logits):
-            return greedy_sample(logits[:, -1]).unsqueeze(-1).contiguous()
+        def forward_decode(k, grp, x):
+            return decode_on([slots[grp]], x)
+
+        def tokens_of(out):
+            if out.dtype == torch.int64:  # already selected by decode_greedy
+                return out.view(-1, 1)
+            return greedy_sample(out[:, -1]).unsqueeze(-1)
+
+        def sample(k, grp, out):
+            return tokens_of(out).contiguous()
 
         host_ids = torch.empty(rows, 1, dtype=torch.int64).pin_memory()
 
-        def sample_host(k, grp, logits):
-            ids = greedy_sample(logits[:, -1]).unsqueeze(-1)
+        def sample_host(k, grp, out):
+            ids = tokens_of(out)
             host_ids.copy_(ids, non_blocking=True)  # the server reads every token
             torch.cuda.current_stream().synchronize()
             return host_ids.to(dev, non_blocking=True)
@@ -245,9 +257,7 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 return stage.forward_slot(slots_w[grp], x, logits="last", check_values=False)
 
             def fwd_dw(k, grp, x):
-                if ring.first:
-                    return stage.decode_multi([slots_w[grp]], None, input_ids=x, logits="last")
-                return stage.decode_multi([slots_w[grp]], x, logits="last")
+                return decode_on([slots_w[grp]], x)
 
             def run_w(n_steps, inputs, fwd, hid):
                 return decode_loop(ring, n_groups, n_steps, inputs, fwd, sample,

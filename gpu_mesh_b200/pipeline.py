@@ -267,6 +267,47 @@ def pipeline_decode_multi(
     return hidden
 
 
+@torch.no_grad()
+def pipeline_decode_greedy(
+    workers: list[B200StageWorker],
+    next_tokens: torch.Tensor,
+    *,
+    cache_keys: Sequence[str | None],
+    return_logits: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``pipeline_decode_multi`` whose last stage also picks every row's
+    greedy token on the device (fused into its lm_head): returns (token ids
+    int64 [rows], logits [rows, 1, V] or None).  The ids equal
+    ``greedy_sample`` of the logits (inference/sampling.py:45-56), which is
+    what the reference's decode loops apply to the returned logits
+    (session.py:245-259, batcher.py:356-388)."""
+    if next_tokens.ndim != 2 or next_tokens.shape[1] != 1:
+        raise ValueError("next_tokens must have shape [rows, 1]")
+    if not workers:
+        raise ValueError("workers must not be empty")
+    max_positions = _max_positions(workers[0])
+    lengths = {}
+    for key in cache_keys:
+        lengths[key] = _checked_lengths(
+            [w.kv_cache_length(key) for w in workers], 1, max_positions,
+            "pipeline_decode_greedy", "pipeline_prefill",
+        )
+    hidden = None
+    try:
+        for i, worker in enumerate(workers[:-1]):
+            hidden = worker.decode_multi(
+                hidden, list(cache_keys), input_ids=next_tokens if i == 0 else None,
+            )
+        return workers[-1].decode_greedy(
+            hidden, list(cache_keys), input_ids=next_tokens if len(workers) == 1 else None,
+            return_logits=return_logits,
+        )
+    except BaseException:
+        for key, lens in lengths.items():
+            _restore_kv_lengths_best_effort(workers, lens, key)
+        raise
+
+
 def _checked_lengths(
     lengths: list[int], query_len: int, max_positions: int | None, name: str, prefill_name: str
 ) -> list[int]:

@@ -376,6 +376,44 @@ class B200Stage:
         )
         return out
 
+    def decode_greedy(
+        self,
+        slots: list[int],
+        x: torch.Tensor | None,
+        *,
+        input_ids: torch.Tensor | None = None,
+        return_logits: bool = False,
+    ) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """``decode_multi`` on the last stage with each row's greedy token
+        chosen on the device (fused into lm_head for the bf16 decode GEMM).
+
+        Returns (token ids int64 [rows] on the stage's device, logits
+        [rows, 1, V] or None).  The ids equal ``greedy_sample`` of the logits.
+        """
+        if not self.has_lm_head:
+            raise ValueError("decode_greedy runs on the last stage")
+        rows = sum(self.kv_batch(s) for s in slots)
+        arr = (ctypes.c_int32 * len(slots))(*slots)
+        ids = None
+        if self.has_embedding:
+            if input_ids is None or input_ids.shape[0] != rows:
+                raise ValueError(f"decode_greedy needs input_ids with {rows} rows")
+            ids = input_ids.to(device=self.device, dtype=torch.int64).contiguous()
+        else:
+            if x is None or x.shape[0] != rows or x.shape[-1] != self.cfg.hidden_size:
+                raise ValueError(f"decode_greedy needs hidden states with {rows} rows")
+            x = x.to(self.device).contiguous()
+        tokens = torch.empty(rows, dtype=torch.int64, device=self.device)
+        logits = (torch.empty((rows, 1, self.cfg.vocab_size), dtype=self.dtype, device=self.device)
+                  if return_logits else None)
+        _lib.check(
+            self._lib.mg_stage_decode_greedy(
+                self.handle, arr, len(slots), _ptr(ids), None if self.has_embedding else _ptr(x),
+                tokens.data_ptr(), _ptr(logits), _stream(self.device),
+            )
+        )
+        return tokens, logits
+
     def profile(self, enable: bool) -> None:
         """Time every launch group with CUDA events (resets on enable)."""
         _lib.check(self._lib.mg_stage_profile(self.handle, int(enable)))

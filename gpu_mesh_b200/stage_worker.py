@@ -172,6 +172,26 @@ class B200StageWorker:
             out = self._model.decode_multi(slots, x, input_ids=input_ids, logits=logits)
         return self._boundary_output(out)
 
+    def decode_greedy(
+        self,
+        hidden: torch.Tensor | None,
+        cache_keys: list[str | None],
+        *,
+        input_ids: torch.Tensor | None = None,
+        return_logits: bool = False,
+    ) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """``decode_multi`` on the last stage returning each row's greedy token
+        (int64 [rows], on the host for transport "cpu") and, if asked, the
+        logits."""
+        with self._inference_lock:
+            slots = [self._slot(k) for k in cache_keys]
+            x = None
+            if hidden is not None:
+                x = self._move_input(hidden)
+            tokens, logits = self._model.decode_greedy(slots, x, input_ids=input_ids,
+                                                       return_logits=return_logits)
+        return self._boundary_output(tokens), (None if logits is None else self._boundary_output(logits))
+
     # ------------------------------------------------------------------
     # KV ownership (stage_worker.py:358-416)
     # ------------------------------------------------------------------

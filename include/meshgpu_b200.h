@@ -195,6 +195,18 @@ int mg_stage_decode_multi(mg_stage* stage, const int32_t* slots, int32_t n_slots
                           const int64_t* input_ids, const void* hidden_in, int32_t out_mode,
                           void* out, void* stream);
 
+/* mg_stage_decode_multi on the last stage with the greedy token of every row
+ * selected on the device: ids_out (device int64 [rows]) receives argmax of
+ * the row's bf16/fp32 logits, the lowest index among equal maxima, as
+ * greedy_sample (inference/sampling.py:45-56) on the logits the reference's
+ * stage returns.  With the bf16 decode GEMM the selection is fused into the
+ * lm_head epilogue; logits_out ([rows, 1, V]) may be NULL when the logits are
+ * not wanted.  Replaces the per-step logits round trip of the reference's
+ * decode loops (session.py:245-259, batcher.py:356-388). */
+int mg_stage_decode_greedy(mg_stage* stage, const int32_t* slots, int32_t n_slots,
+                           const int64_t* input_ids, const void* hidden_in, int64_t* ids_out,
+                           void* logits_out, void* stream);
+
 /* Read and clear the stage's device error word (waits for `stream`).
  * Returns MG_EDEVICE with a message when a kernel met an out-of-range token
  * id or position since the last check. */
