@@ -71,6 +71,8 @@ SHAPES = [
     (32, 128256, 4096), (32, 4096, 4096),
     # ... and prefill shapes on the tcgen05 GEMM, including ragged M.
     (33, 4096, 4096), (100, 688, 256), (128, 6144, 4096), (300, 4096, 14336), (1024, 1024, 2560),
+    # several tiles per CTA of the persistent GEMM, both tile orders, ragged N
+    (2048, 4096, 4096), (4096, 1024, 2048), (1500, 2000, 512),
 ]
 
 
