@@ -23,6 +23,35 @@ __device__ __forceinline__ int visible(const AttnArgs& a, const RowDesc& rd, int
   return (int)(pos + 1 < (int64_t)total ? pos + 1 : (int64_t)total);
 }
 
+// Query tiles of the prefill kernels: a work item is (cache row, KV head,
+// tile of tq = 128 / G tokens x the G heads sharing the KV head), heaviest
+// (latest) tiles first.
+struct PrefillPlan {
+  int tq;      // tokens of a tile (128 / G)
+  int ntiles;  // query tiles per cache row
+  long long items;
+};
+
+// Item i (heaviest first): query tile, cache row, KV head.
+__device__ __forceinline__ void item_of(const AttnArgs& a, const PrefillPlan& pl, long long i, int& qt, int& b,
+                                        int& h) {
+  const long long bh = (long long)a.B * a.nkv;
+  qt = pl.ntiles - 1 - (int)(i / bh);
+  const int rem = (int)(i % bh);
+  b = rem / a.nkv;
+  h = rem % a.nkv;
+}
+
+// Keys the tile's last token sees: the item's chunk count follows from it.
+__device__ __forceinline__ int tile_keys(const AttnArgs& a, const RowDesc& rd, const PrefillPlan& pl, int b,
+                                         int qt) {
+  int s_hi = (qt + 1) * pl.tq;
+  if (s_hi > a.S) s_hi = a.S;
+  int kmax = 0;
+  for (int s = qt * pl.tq; s < s_hi; ++s) kmax = max(kmax, visible(a, rd, b * a.S + s, s));
+  return kmax;
+}
+
 __device__ __forceinline__ void tma_load_2d_gmap(void* dst, uint64_t tmap, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "

@@ -47,32 +47,6 @@ struct PrefillLayout {
   static constexpr int bytes(int stages) { return stages * kStage + 2 * kMaxStagesP * 8 + 16 + 1024; }
 };
 
-struct PrefillPlan {
-  int tq;      // tokens of a tile (128 / G)
-  int ntiles;  // query tiles per cache row
-  long long items;
-};
-
-// Item i (heaviest first): query tile, cache row, KV head.
-__device__ __forceinline__ void item_of(const AttnArgs& a, const PrefillPlan& pl, long long i, int& qt, int& b,
-                                        int& h) {
-  const long long bh = (long long)a.B * a.nkv;
-  qt = pl.ntiles - 1 - (int)(i / bh);
-  const int rem = (int)(i % bh);
-  b = rem / a.nkv;
-  h = rem % a.nkv;
-}
-
-// Keys the tile's last token sees: the item's chunk count follows from it.
-__device__ __forceinline__ int tile_keys(const AttnArgs& a, const RowDesc& rd, const PrefillPlan& pl, int b,
-                                         int qt) {
-  int s_hi = (qt + 1) * pl.tq;
-  if (s_hi > a.S) s_hi = a.S;
-  int kmax = 0;
-  for (int s = qt * pl.tq; s < s_hi; ++s) kmax = max(kmax, visible(a, rd, b * a.S + s, s));
-  return kmax;
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreadsP, 1) attn_prefill_kernel(AttnArgs a, PrefillPlan pl, int stages) {
   using L = PrefillLayout<D>;

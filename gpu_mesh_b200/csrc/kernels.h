@@ -235,8 +235,6 @@ struct AttnArgs {
   // launch starts and zero again when it ends.
   int* counters;
   size_t counters_elems;
-  // kEpiGreedy: the selection buffers (device pointers; unused otherwise).
-  Greedy greedy{nullptr, nullptr, nullptr};
 };
 size_t attention_scratch_elems(int M, int nq, int D, int max_keys);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
@@ -250,6 +248,10 @@ bool attention_tc_applicable(int dtype, int D, int G);
 // bf16, head_dim 64 or 128, G dividing 16, S >= 8 query tokens per row.
 bool attention_prefill_applicable(int dtype, int D, int G, int S);
 cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t s);
+// The same work on tcgen05 (k_attention_prefill_tc.cu): scores and output in
+// TMEM, one softmax thread per query row.
+bool attention_prefill_tc_applicable(int dtype, int D, int G, int S);
+cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s);
 size_t attention_tc_scratch_elems(int nq, int D);
 cudaError_t launch_attention_tc(const AttnArgs& a, int splits, cudaStream_t s);
 
