@@ -266,6 +266,7 @@ def run_single(args) -> None:
     t1.record()
     torch.cuda.synchronize()
     prefill_ms = t0.elapsed_time(t1)
+    stage.check_device()  # a kernel that gave up waiting would make every number below meaningless
     ids = torch.cat(first).unsqueeze(-1)
 
     def step(ids):
@@ -314,6 +315,7 @@ def run_single(args) -> None:
     e3.record()
     torch.cuda.synchronize()
     e2e_ms = e2.elapsed_time(e3)
+    stage.check_device()
 
     lin = prof["linear_decode"]
     att = prof["attention"]

@@ -9,18 +9,23 @@
 //     TMA through the slot's tensor map (box 128 keys x 64 dims, 128-byte
 //     swizzle, no multicast) into a 2-stage ring;
 //   * warp 1, one lane: issues tcgen05.mma.  S = Q·Kᵀ (M = 128 query rows,
-//     N = 128 keys, K = D; Q and K both K-major) into one of two TMEM score
-//     buffers, then O += P·V (M = 128 rows, N = D, K = 128 keys; P K-major,
-//     V read MN-major straight from its TMA box) into the TMEM output.  The
-//     score product of chunk j + 1 is issued before the value product of
-//     chunk j, so it overlaps that chunk's softmax;
-//   * warps 2-5: one thread per query row (its TMEM lane).  They write the
-//     tile's query rows into shared memory, and per chunk read their row of
-//     S, mask it by the reference's visible-key rule, keep the online softmax
-//     in base 2 (m' = max(m, max S), P = exp2(S - m'), l = l·exp2(m - m') +
-//     ΣP), rescale their row of O in TMEM when the maximum moved, and write
-//     P as bf16 high + low parts (two MMAs, so the weights keep fp32
-//     accuracy) for the value product.  At the end they write O / l.
+//     N = 128 keys, K = D; Q and K K-major in shared memory) into one of two
+//     TMEM score buffers; O += P·V (M = 128 rows, N = D, K = 128 keys) into
+//     the TMEM output, with P read from TMEM (where the softmax left it, in
+//     the chunk's score buffer) and V read MN-major straight from its TMA
+//     box.  The score product of chunk j + 1 is issued before the value
+//     product of chunk j, so it overlaps that chunk's softmax;
+//   * warps 2-9: two threads per query row (its TMEM lane), each owning 64
+//     of a chunk's 128 keys and half of the head dims; the pair exchanges
+//     its partial row maxima through shared memory.  They write the tile's
+//     query rows into shared memory, and per chunk read their part of S's
+//     row, mask it by the reference's visible-key rule and keep the online
+//     softmax in base 2 (P = 2^(S·scale2 - m·scale2), l = l·α + ΣP).  The
+//     running maximum m is moved only when a row's scores exceed it by more
+//     than 2^8, and only then is the row of O in TMEM rescaled by α (the
+//     result O / l does not depend on which m is used).  P goes back into
+//     TMEM as bf16 high + low parts (two MMAs, so the weights keep fp32
+//     accuracy).  At the end they write O / l.
 // Value rows at or past the cache end were never written: they are cleared
 // in shared memory before the value product (P is 0 there, but 0 * NaN is
 // not).  Every wait is bounded (code 3 in the error word on expiry); on
@@ -30,6 +35,7 @@
 #include "attn_tc_common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
+
 
 namespace mg {
 namespace {
@@ -41,7 +47,8 @@ using bf16 = __nv_bfloat16;
 constexpr int kRowsT = 128;              // query rows of a tile = TMEM lanes
 constexpr int kChunkT = kKvBoxKeys;      // keys per chunk (128)
 constexpr int kBoxT = kKvBoxKeys * 128;  // a 128-row x 128-byte swizzled block (16 KB)
-constexpr int kThreadsT = 192;
+constexpr int kSoftWarps = 8;            // two per TMEM lane quadrant, 64 keys each
+constexpr int kThreadsT = 64 + 32 * kSoftWarps;
 constexpr int kColS = 0;                 // TMEM columns: scores [0, 256) in two buffers,
 constexpr int kColO = 256;               // the output [256, 256 + D)
 
@@ -49,15 +56,13 @@ template <int D>
 struct TcPrefillLayout {
   static constexpr int kDB = D / 64;       // 64-wide blocks of D
   static constexpr int kQ = kDB * kBoxT;   // query tile (A of S)
-  static constexpr int kP = 2 * kBoxT;     // P tile (128 rows x 128 keys), each of high / low
   static constexpr int kKV = kDB * kBoxT;  // keys (or values) of a chunk
   static constexpr int kStages = 2;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffPh = kOffQ + kQ;
-  static constexpr int kOffPl = kOffPh + kP;
-  static constexpr int kOffKV = kOffPl + kP;
+  static constexpr int kOffKV = kOffQ + kQ;
   static constexpr int kOffBar = kOffKV + kStages * 2 * kKV;
-  static constexpr int kBytes = kOffBar + 256 + 1024;
+  static constexpr int kOffX = kOffBar + 128;          // [2 chunk parities][2 halves][128 rows] floats
+  static constexpr int kBytes = kOffX + 2048 + 1024;
 };
 
 // Shared-memory descriptor of an MN-major operand with 128-byte swizzle: 64
@@ -75,6 +80,30 @@ __device__ __forceinline__ int swz_off(int r, int c) {
   return (c >> 3) * kBoxT + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
+// D (TMEM) += A (TMEM, M lanes x K bf16 packed two per column) · B (shared).
+__device__ __forceinline__ void mma_bf16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Two floats to a bf16 pair (round to nearest even), `lo` in the low half.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x on the special-function unit (ex2.approx.ftz.f32: -inf -> +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
 }
@@ -87,19 +116,18 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sq = smem + L::kOffQ;
-  uint8_t* sph = smem + L::kOffPh;
-  uint8_t* spl = smem + L::kOffPl;
   uint8_t* skv = smem + L::kOffKV;  // stage s: keys at skv + 2·s·kKV, values kKV after them
   uint64_t* bars = (uint64_t*)(smem + L::kOffBar);
   uint64_t* kvfull = bars;       // [2] chunk landed
   uint64_t* kvempty = bars + 2;  // [2] chunk's value product done
   uint64_t* sfull = bars + 4;    // [2] scores ready in TMEM buffer
-  uint64_t* pready = bars + 6;   // P written, O rescaled (4 warps)
+  uint64_t* pready = bars + 6;   // P written, O rescaled (softmax warps)
   uint64_t* odone = bars + 7;    // value product done
-  uint64_t* qready = bars + 8;   // query tile written (4 warps)
+  uint64_t* qready = bars + 8;   // query tile written (softmax warps)
   uint64_t* drain = bars + 9;    // every MMA finished
   uint32_t* tmem_holder = (uint32_t*)(bars + 10);
   volatile int* abort_flag = (volatile int*)(tmem_holder + 1);
+  float* xch = (float*)(smem + L::kOffX);  // a row's partial maxima (then sums) of the two halves
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -108,9 +136,9 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       mbar_init(&kvempty[s], 1);
       mbar_init(&sfull[s], 1);
     }
-    mbar_init(pready, 4);
+    mbar_init(pready, kSoftWarps);
     mbar_init(odone, 1);
-    mbar_init(qready, 4);
+    mbar_init(qready, kSoftWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -159,25 +187,34 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
   } else if (warp == 1) {
     if (lane == 0) {
       // MMA issuer.  Per item: wait for the query tile; per chunk n: the
-      // score product into TMEM buffer n & 1, then the value product of chunk
-      // n - 1 once its P is written (and of the item's last chunk at the end).
+      // score product into TMEM buffer n & 1 (once the value product of chunk
+      // n - 2, which read its P from that buffer, has finished), then the
+      // value product of chunk n - 1 once its P is written (and of the item's
+      // last chunk at the end).
       constexpr uint32_t idS = instr_desc(kChunkT);
       constexpr uint32_t idPV = instr_desc(D) | (1u << 16);  // B (the values) MN-major
       long long n = 0;
       int it = 0;
+      // odone phases this thread has seen complete, waited strictly in order
+      // and never after the next value product was issued (a parity wait
+      // two phases behind would match the wrong phase).
+      long long o_seen = -1;
+      auto wait_odone = [&](long long upto) -> bool {
+        for (; o_seen < upto; ++o_seen)
+          if (!mbar_wait(odone, (int)((o_seen + 1) & 1), a.err)) return false;
+        return true;
+      };
       auto value_product = [&](long long m, bool first) -> bool {
         if (!mbar_wait(pready, (int)(m & 1), a.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint8_t* v = skv + (int)(m & 1) * 2 * L::kKV + L::kKV;
+        const uint32_t pt = tmem + kColS + (uint32_t)(m & 1) * kChunkT;  // P high, then P low 64 columns on
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {  // P high, then P low
-          const uint8_t* pp = part ? spl : sph;
+        for (int part = 0; part < 2; ++part) {
 #pragma unroll
-          for (int kk = 0; kk < kChunkT / 16; ++kk) {
-            const uint64_t da = smem_desc(pp + (kk >> 2) * kBoxT) + (uint64_t)((kk & 3) * 2);
-            const uint64_t db = smem_desc_mn(v + kk * 16 * 128, kBoxT);
-            mma_bf16(tmem + kColO, da, db, idPV, (first && part == 0 && kk == 0) ? 0u : 1u);
-          }
+          for (int kk = 0; kk < kChunkT / 16; ++kk)
+            mma_bf16_ta(tmem + kColO, pt + part * (kChunkT / 2) + kk * 8, smem_desc_mn(v + kk * 16 * 128, kBoxT),
+                        idPV, (first && part == 0 && kk == 0) ? 0u : 1u);
         }
         mma_commit(odone);
         mma_commit(&kvempty[m & 1]);
@@ -195,7 +232,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         }
         ++it;
         for (int ch = 0; ch < nch; ++ch, ++n) {
-          if (!mbar_wait(&kvfull[n & 1], (int)(n >> 1) & 1, a.err) || *abort_flag) {
+          if (!mbar_wait(&kvfull[n & 1], (int)(n >> 1) & 1, a.err) || !wait_odone(n - 2) || *abort_flag) {
             ok = false;
             break;
           }
@@ -213,18 +250,46 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
             break;
           }
         }
-        if (ok && nch > 0 && !value_product(n - 1, nch == 1)) ok = false;
+        if (ok && nch > 0 && (!wait_odone(n - 2) || !value_product(n - 1, nch == 1))) ok = false;
       }
       if (!ok) *abort_flag = 1;
       mma_commit(drain);  // arrives once every MMA issued above has finished
     }
   } else {
-    // Softmax warps 2-5: warp w owns TMEM lanes 32·(w % 4) .. + 31, one
-    // query row per thread.
+    // Softmax warps 2-9: warp w owns TMEM lanes 32·(w % 4) .. + 31 (one query
+    // row per thread) and half (w - 2) / 4 of every chunk's keys (and of the
+    // head dims for the query, output and rescale).
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
     const float scale2 = a.scale * 1.4426950408889634f;
+    constexpr int kHK = kChunkT / 2;  // keys of this half
+    constexpr int kHD = D / 2;        // dims of this half
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + q4) : "memory"); };
+    // The two warps of a row pair decide together whether a wait failed, so
+    // neither is left at a pair barrier the other has abandoned.
+    auto pair_any = [&](bool pred) -> bool {
+      uint32_t res;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "barrier.red.or.pred q, %2, 64, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(res)
+          : "r"((uint32_t)pred), "r"(1 + q4)
+          : "memory");
+      return res != 0;
+    };
+    // Value products this warp has seen finish: odone phases are waited in
+    // order, never skipping one (a parity wait could otherwise match an older
+    // phase).
+    long long o_seen = -1;
+    auto wait_odone = [&](long long upto) -> bool {
+      for (; o_seen < upto; ++o_seen)
+        if (!warp_wait(odone, (int)((o_seen + 1) & 1), a.err)) return false;
+      return true;
+    };
     long long n = 0;
     bool ok = true;
     for (long long i = blockIdx.x; i < pl.items && ok; i += gridDim.x) {
@@ -237,12 +302,12 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       const bool valid = r / G < pl.tq && s_tok < a.S;
       const int vis = valid ? visible(a, rd, b * a.S + s_tok, s_tok) : 0;
       const int tot = rd.past + a.S;  // keys written so far
-      // The query row into the tile (zeros for rows past the sequence).
+      // This half of the query row into the tile (zeros for rows past the sequence).
       {
         const uint4* src = reinterpret_cast<const uint4*>(
             (const bf16*)a.q + (((size_t)b * a.S + (valid ? s_tok : 0)) * a.nq + (size_t)h * G + g) * D);
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
+        for (int c = half * (kHD / 8); c < (half + 1) * (kHD / 8); ++c) {
           const uint4 val = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
           *reinterpret_cast<uint4*>(sq + swz_off(r, c)) = val;
         }
@@ -251,77 +316,103 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       __syncwarp();
       if (lane == 0) mbar_arrive(qready);
 
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY, l = 0.f;  // m: the running maximum P is taken against (raw scores); l: this half's sum
       for (int ch = 0; ch < nch; ++ch, ++n) {
         const int sb = (int)(n & 1);
         // scores ready; the chunk's load is complete too (it orders the TMA
         // writes before the value clearing below)
-        if (!warp_wait(&sfull[sb], (int)(n >> 1) & 1, a.err) ||
-            !warp_wait(&kvfull[sb], (int)(n >> 1) & 1, a.err)) {
+        const bool late = !warp_wait(&sfull[sb], (int)(n >> 1) & 1, a.err) ||
+                          !warp_wait(&kvfull[sb], (int)(n >> 1) & 1, a.err);
+        if (pair_any(late)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float sc[kChunkT];
+        float sc[kHK];
 #pragma unroll
-        for (int c4 = 0; c4 < kChunkT / 32; ++c4)
-          tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + c4 * 32, sc + c4 * 32);
-        const int nv = vis - ch * kChunkT;  // visible keys of this chunk for this row
-        float mx = m;
+        for (int c4 = 0; c4 < kHK / 32; ++c4)
+          tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * kHK + c4 * 32, sc + c4 * 32);
+        const int nv = vis - ch * kChunkT - half * kHK;  // visible keys of this half for this row
+        // Row maximum of the raw scores (the scale is positive, so it commutes
+        // with the maximum), as a tree; invisible keys become -inf.
+        if (!__all_sync(0xffffffffu, nv >= kHK)) {
 #pragma unroll
-        for (int c = 0; c < kChunkT; ++c) {
-          sc[c] = c < nv ? sc[c] * scale2 : -INFINITY;
-          mx = fmaxf(mx, sc[c]);
+          for (int c = 0; c < kHK; ++c) sc[c] = c < nv ? sc[c] : -INFINITY;
         }
-        const float alpha = (m == -INFINITY) ? 1.f : exp2f(m - mx);
-        float sum = 0.f;
+        float t8[8];
 #pragma unroll
-        for (int c = 0; c < kChunkT; ++c) {
-          sc[c] = sc[c] == -INFINITY ? 0.f : exp2f(sc[c] - mx);
-          sum += sc[c];
+        for (int j = 0; j < 8; ++j) t8[j] = sc[j];
+#pragma unroll
+        for (int c = 8; c < kHK; ++c) t8[c & 7] = fmaxf(t8[c & 7], sc[c]);
+        const float pm = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
+                               fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+        float* xs = xch + (size_t)(sb * 2) * kRowsT;
+        xs[half * kRowsT + r] = pm;
+        pair_sync();  // (double-buffered by chunk parity: one barrier per chunk)
+        const float mt = fmaxf(pm, xs[(1 - half) * kRowsT + r]);
+        // Move the maximum only when the scores outgrow it by 2^8.
+        float m_new = m;
+        bool moved = false;
+        if (m == -INFINITY) {
+          m_new = mt;
+        } else if ((mt - m) * scale2 > 8.f) {
+          m_new = mt;
+          moved = true;
         }
-        l = l * alpha + sum;
-        m = mx;
-        if (ch > 0) {
-          // The previous value product is done: O is stable and P is free.
-          if (!warp_wait(odone, (int)((n - 1) & 1), a.err)) {
-            ok = false;
-            break;
-          }
+        const float alpha = moved ? ex2_approx((m - m_new) * scale2) : 1.f;
+        // The previous value product is done before this chunk's P goes into
+        // TMEM and before O is rescaled.  Waiting for it here (not for the
+        // one before) also keeps this thread's odone waits within one phase
+        // of the barrier: value product n can only start after this chunk's
+        // P is handed over.
+        const bool rescale = __any_sync(0xffffffffu, moved);
+        if (pair_any(!wait_odone(n - 1))) {
+          ok = false;
+          break;
+        }
+        if (rescale) {
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-            for (int c4 = 0; c4 < D / 32; ++c4) {
-              float o[32];
-              tmem_ld32(tmem + lanes + kColO + c4 * 32, o);
+          for (int c4 = 0; c4 < kHD / 32; ++c4) {
+            float o[32];
+            tmem_ld32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] *= alpha;
-              tmem_st32(tmem + lanes + kColO + c4 * 32, o);
-            }
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
           }
         }
-        // Value rows past the written keys: clear them before the product.
+        // P = 2^(S·scale2 - m·scale2): one fused multiply-add and one ex2 per
+        // key (invisible keys are -inf and give 0).
+        const float mb = m_new == -INFINITY ? 0.f : m_new * scale2;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t8[j] = 0.f;
+#pragma unroll
+        for (int c = 0; c < kHK; ++c) {
+          sc[c] = ex2_approx(fmaf(sc[c], scale2, -mb));
+          t8[c & 7] += sc[c];
+        }
+        l = l * alpha + (((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7])));
+        m = m_new;
+        // Value rows past the written keys: clear this half of them before the product.
         if (ch * kChunkT + kChunkT > tot && ch * kChunkT + r >= tot) {
           uint8_t* v = skv + sb * 2 * L::kKV + L::kKV;
 #pragma unroll
-          for (int db = 0; db < DB; ++db)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              *reinterpret_cast<uint4*>(v + db * kBoxT + r * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = half * (kHD / 8); c < (half + 1) * (kHD / 8); ++c)
+            *reinterpret_cast<uint4*>(v + (c >> 3) * kBoxT + r * 128 + (c & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
-        // P = high + low bf16 parts, this row of the K-major P tiles.
+        // P as bf16 high + low parts into the chunk's score buffer (its scores
+        // are in registers on both halves: the pair barrier above): high at
+        // columns [32·half, +32), low 64 columns on.
+        {
+          float hw[32], lw[32];
 #pragma unroll
-        for (int c8 = 0; c8 < kChunkT / 8; ++c8) {
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x0 = sc[8 * c8 + 2 * e], x1 = sc[8 * c8 + 2 * e + 1];
-            hw[e] = pack2(x0, x1);
-            lw[e] = pack2(x0 - lo_bf16(hw[e]), x1 - hi_bf16(hw[e]));
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t hv = cvt_bf16x2(sc[2 * j], sc[2 * j + 1]);
+            hw[j] = __uint_as_float(hv);
+            lw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j] - lo_bf16(hv), sc[2 * j + 1] - hi_bf16(hv)));
           }
-          const int off = swz_off(r, c8);
-          *reinterpret_cast<uint4*>(sph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(spl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, hw);
+          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + half * 32, lw);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -329,21 +420,30 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         if (lane == 0) mbar_arrive(pready);
       }
       if (!ok) break;
-      // O / l for this row.
+      // The row sum from both halves, then O / l for this half of the dims.
+      {
+        float* xs = xch + (size_t)((n & 1) * 2) * kRowsT;
+        xs[half * kRowsT + r] = l;
+        pair_sync();
+        const float lo = xs[(1 - half) * kRowsT + r];
+        pair_sync();  // read before the next item's chunk of the same parity writes
+        l += lo;
+      }
       if (nch > 0) {
-        if (!warp_wait(odone, (int)((n - 1) & 1), a.err)) {
+        if (pair_any(!wait_odone(n - 1))) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       }
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const float lrow = l;
+      const float inv = lrow > 0.f ? 1.0f / lrow : 0.f;
       bf16* out = (bf16*)a.out + (((size_t)b * a.S + (valid ? s_tok : 0)) * a.nq + (size_t)h * G + g) * D;
 #pragma unroll 1
-      for (int c4 = 0; c4 < D / 32; ++c4) {
+      for (int c4 = 0; c4 < kHD / 32; ++c4) {
         float o[32];
         if (nch > 0) {
-          tmem_ld32(tmem + lanes + kColO + c4 * 32, o);
+          tmem_ld32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0.f;
@@ -356,7 +456,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
             w.y = pack2(o[8 * e8 + 2] * inv, o[8 * e8 + 3] * inv);
             w.z = pack2(o[8 * e8 + 4] * inv, o[8 * e8 + 5] * inv);
             w.w = pack2(o[8 * e8 + 6] * inv, o[8 * e8 + 7] * inv);
-            *reinterpret_cast<uint4*>(out + c4 * 32 + 8 * e8) = w;
+            *reinterpret_cast<uint4*>(out + half * kHD + c4 * 32 + 8 * e8) = w;
           }
         }
       }

@@ -21,9 +21,15 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 8), (64, 32, 4), (128, 8, 8), (64, 16, 8)],
-                         ids=["d128-g4", "d64-g8", "d128-g1", "d64-g2"])
-@pytest.mark.parametrize("T,S", [(0, 8), (0, 200), (5, 33), (130, 77), (1000, 129)])
+CASES = [(D, nq, nkv, T, S)
+         for D, nq, nkv in [(128, 32, 8), (64, 32, 4), (128, 8, 8), (64, 16, 8)]
+         for T, S in [(0, 8), (0, 200), (5, 33), (130, 77), (1000, 129)]]
+# Several work items per CTA (more than 148 items), tiles of up to 10 chunks.
+CASES += [(128, 32, 8, 0, 1100), (128, 32, 8, 300, 600), (64, 32, 4, 700, 400)]
+
+
+@pytest.mark.parametrize("D,nq,nkv,T,S", CASES,
+                         ids=[f"d{c[0]}-g{c[1] // c[2]}-T{c[3]}-S{c[4]}" for c in CASES])
 def test_prefill_attention_matches_oracle(D, nq, nkv, T, S):
     cfg = LlamaConfig(vocab_size=256, hidden_size=512, intermediate_size=1024, num_hidden_layers=1,
                       num_attention_heads=nq, num_key_value_heads=nkv, head_dim=D,
