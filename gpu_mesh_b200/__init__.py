@@ -18,6 +18,7 @@ from gpu_mesh_b200.pipeline import (
 from gpu_mesh_b200.sampling import SamplingParams, greedy_sample, make_sampling_generator, top_p_sample
 from gpu_mesh_b200.stage import B200Stage
 from gpu_mesh_b200.stage_worker import B200StageWorker, ForwardResult, StageContext
+from gpu_mesh_b200.wire import tensor_from_wire, tensor_wire_parts
 
 __all__ = [
     "B200Stage",
@@ -41,5 +42,7 @@ __all__ = [
     "pipeline_prefill",
     "pipeline_prefill_async",
     "split_layers",
+    "tensor_from_wire",
+    "tensor_wire_parts",
     "top_p_sample",
 ]
