@@ -63,6 +63,40 @@ def llama3_8b(layers: int = 32):
     )
 
 
+# The scope's other benchmark architectures (--model): batch, prompt and
+# sampling of their configurations; a step is one decode token for every row.
+MODELS = {
+    "llama3-8b": dict(arch="Llama-3-8B", layers=32, micro=8, micro_batches=4, prompt=1024, sampling="greedy"),
+    "tinyllama-1.1b": dict(arch="TinyLlama-1.1B", layers=22, micro=8, micro_batches=1, prompt=512,
+                           sampling="greedy"),
+    "qwen3-4b": dict(arch="Qwen3-4B", layers=36, micro=16, micro_batches=1, prompt=2048,
+                     sampling="top-p (T 0.7, p 0.9, seeded)"),
+}
+TOP_P = (0.7, 0.9)
+
+
+def model_config(name: str, layers: int | None = None):
+    from gpu_mesh_b200.config import LlamaConfig
+
+    n = layers or MODELS[name]["layers"]
+    if name == "llama3-8b":
+        return llama3_8b(n)
+    if name == "tinyllama-1.1b":
+        return LlamaConfig(vocab_size=32000, hidden_size=2048, intermediate_size=5632, num_hidden_layers=n,
+                           num_attention_heads=32, num_key_value_heads=4, head_dim=64,
+                           max_position_embeddings=4096, rms_norm_eps=1e-5, rope_theta=10000.0)
+    return LlamaConfig(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=n,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192,
+                       rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=True, qk_norm=True,
+                       mask_policy="cache")
+
+
+def metric_for(args) -> str:
+    if args.model == "llama3-8b":
+        return METRIC
+    return f"decode tok/s ({MODELS[args.model]['arch']} arch, B200 stages)"
+
+
 def peaks() -> tuple[float, float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -129,12 +163,12 @@ def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cfg = llama3_8b(args.layers)
+    cfg = model_config(args.model, args.layers)
     base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=max(1, min(args.steps, 2)))
     steps = args.steps
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": metric_for(args),
         "value": base["value"],
         "unit": "tok/s",
         "n_gpus": args.gpus,
@@ -154,9 +188,11 @@ def run_reference_arm(args) -> None:
 
 
 def workload_config(args) -> dict:
-    layers = "" if args.layers == 32 else f" cut to {args.layers} layers (profiling case)"
+    m = MODELS[args.model]
+    layers = "" if args.layers == m["layers"] else f" cut to {args.layers} layers (profiling case)"
+    sampling = "greedy" if m["sampling"] == "greedy" else m["sampling"]
     return {
-        "workload": f"Llama-3-8B-architecture{layers} bf16 greedy decode, batch "
+        "workload": f"{m['arch']}-architecture{layers} bf16 {sampling} decode, batch "
                     f"{args.micro * args.micro_batches} as {args.micro_batches} micro-batches of "
                     f"{args.micro}, {args.prompt}-token prompts",
         "layers": args.layers,
@@ -165,7 +201,7 @@ def workload_config(args) -> dict:
         "prompt": args.prompt,
         "stages": args.gpus,
         "parallelism": f"pp{args.gpus}",
-        "l2": "inputs larger than L2: every step streams all weights (16 GB) and the KV caches",
+        "l2": "inputs larger than L2: every step streams all weights and the KV caches",
     }
 
 
@@ -237,11 +273,15 @@ def long_context(hbm: float, *, rows: int = 64, context: int = 8192, layers: int
 
 def run_single(args) -> None:
     from gpu_mesh_b200 import _lib, build_pipeline, greedy_sample
-    from gpu_mesh_b200.pipeline import pipeline_decode_greedy
+    from gpu_mesh_b200.pipeline import pipeline_decode_greedy, pipeline_decode_multi
+
+    from gpu_mesh_b200.sampling import top_p_sample
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cfg = llama3_8b(args.layers)
+    cfg = model_config(args.model, args.layers)
+    greedy = MODELS[args.model]["sampling"] == "greedy"
+    sample_gen = torch.Generator(device=dev).manual_seed(1234)
     hbm, tflops, peak_kind = peaks()
     workers = build_pipeline(cfg, 1, [dev], transport="local_cuda", dtype=torch.bfloat16, check_values=False)
     w = workers[0]
@@ -270,7 +310,11 @@ def run_single(args) -> None:
     ids = torch.cat(first).unsqueeze(-1)
 
     def step(ids):
-        tokens, _ = w.decode_greedy(None, keys, input_ids=ids)  # selection fused into lm_head
+        if greedy:
+            tokens, _ = w.decode_greedy(None, keys, input_ids=ids)  # selection fused into lm_head
+        else:
+            logits = w.decode_multi(None, keys, input_ids=ids, logits="last")
+            tokens = top_p_sample(logits[:, -1], *TOP_P, generator=sample_gen)
         return tokens.unsqueeze(-1)
 
     for _ in range(args.warmup):
@@ -307,7 +351,11 @@ def run_single(args) -> None:
     e2.record()
     for _ in range(args.steps):
         d_ids = host_ids.to(dev, non_blocking=True)
-        tok, _ = pipeline_decode_greedy(workers, d_ids, cache_keys=keys)
+        if greedy:
+            tok, _ = pipeline_decode_greedy(workers, d_ids, cache_keys=keys)
+        else:
+            logits = pipeline_decode_multi(workers, d_ids, cache_keys=keys)
+            tok = top_p_sample(logits[:, -1], *TOP_P, generator=sample_gen)
         tok = tok.unsqueeze(-1)
         host_out.copy_(tok, non_blocking=True)
         torch.cuda.current_stream().synchronize()
@@ -331,14 +379,16 @@ def run_single(args) -> None:
         wk.close()
     del workers, w, stage
     torch.cuda.empty_cache()
-    longctx = None if args.no_long_context else long_context(hbm)
+    longctx = None if args.no_long_context or args.model != "llama3-8b" else long_context(hbm)
 
     base = None
     if not args.no_cpu_baseline:
         base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=2)
 
+    traffic = NCU_TRAFFIC if args.model == "llama3-8b" else {
+        k: {"dram_bytes": None, "algorithmic_bytes": None, "launches": None} for k in NCU_TRAFFIC}
     line = {
-        "metric": METRIC,
+        "metric": metric_for(args),
         "value": value,
         "unit": "tok/s",
         "n_gpus": 1,
@@ -358,9 +408,9 @@ def run_single(args) -> None:
             "peak": hbm,
             "unit": "GB/s",
             "frac": lin_gbs / hbm,
-            "traffic": NCU_TRAFFIC["gemv_tc"]["dram_bytes"],
-            "traffic_algorithmic": NCU_TRAFFIC["gemv_tc"]["algorithmic_bytes"],
-            "traffic_launches": NCU_TRAFFIC["gemv_tc"]["launches"],
+            "traffic": traffic["gemv_tc"]["dram_bytes"],
+            "traffic_algorithmic": traffic["gemv_tc"]["algorithmic_bytes"],
+            "traffic_launches": traffic["gemv_tc"]["launches"],
             "peak_kind": peak_kind,
             "share_of_step": lin["ms"] / prof_ms if prof_ms else None,
         },
@@ -371,9 +421,9 @@ def run_single(args) -> None:
             "peak": hbm,
             "unit": "GB/s",
             "frac": att_gbs / hbm,
-            "traffic": NCU_TRAFFIC["attn_tc"]["dram_bytes"],
-            "traffic_algorithmic": NCU_TRAFFIC["attn_tc"]["algorithmic_bytes"],
-            "traffic_launches": NCU_TRAFFIC["attn_tc"]["launches"],
+            "traffic": traffic["attn_tc"]["dram_bytes"],
+            "traffic_algorithmic": traffic["attn_tc"]["algorithmic_bytes"],
+            "traffic_launches": traffic["attn_tc"]["launches"],
             "share_of_step": att["ms"] / prof_ms if prof_ms else None,
         },
         "step_roofline": {
@@ -408,17 +458,22 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--prompt", type=int, default=1024)
-    ap.add_argument("--micro", type=int, default=8)
-    ap.add_argument("--micro-batches", type=int, default=4)
-    ap.add_argument("--layers", type=int, default=32,
-                    help="decoder layers (32 = Llama-3-8B; fewer only for profiling captures)")
+    ap.add_argument("--model", choices=sorted(MODELS), default="llama3-8b",
+                    help="architecture and its configuration (batch, prompt, sampling)")
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--micro", type=int, default=None)
+    ap.add_argument("--micro-batches", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers (default: the model's; fewer only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-weak", action="store_true",
                     help="N > 1: skip the weak-scaling measurement (N groups of 32 rows in flight)")
     ap.add_argument("--no-long-context", action="store_true",
                     help="skip the long-context attention measurement (64 rows x 8192 positions)")
     args = ap.parse_args()
+    for k in ("prompt", "micro", "micro_batches", "layers"):
+        if getattr(args, k) is None:
+            setattr(args, k, MODELS[args.model][k])
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
@@ -429,7 +484,9 @@ def main() -> None:
         return
     from gpu_mesh_b200.dist import run_pipeline_bench
 
-    run_pipeline_bench(args, llama3_8b(args.layers), METRIC, workload_config(args), peaks(), NCU_TRAFFIC)
+    run_pipeline_bench(args, model_config(args.model, args.layers), metric_for(args), workload_config(args), peaks(),
+                       NCU_TRAFFIC if args.model == "llama3-8b" else None,
+                       top_p=None if MODELS[args.model]["sampling"] == "greedy" else TOP_P)
 
 
 if __name__ == "__main__":

@@ -25,6 +25,7 @@ namespace {
 
 constexpr int kSampleThreads = 1024;
 
+
 template <typename T>
 __device__ __forceinline__ float logit_at(const T* row, int i) {
   return ldf<T>(row + i);
@@ -140,17 +141,26 @@ __device__ __forceinline__ float scaled(const T* row, int i, float temperature) 
   return logit_at<T>(row, i) / temperature;
 }
 
+// The row's probabilities are computed once into `pr` (fp32, the row's slice
+// of a scratch buffer, 16-byte aligned); every search pass then reads them
+// back (L2) instead of recomputing an exponential per token.  Thread t owns
+// the 4-element groups t, t + blockDim, ... in every pass, so it only reads
+// values it wrote itself, except in the final rank scan (after a barrier).
 template <typename T>
 __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restrict__ logits,
                                                                int vocab, int64_t stride,
                                                                float temperature, float top_p,
                                                                const float* __restrict__ uniforms,
-                                                               int64_t* __restrict__ ids) {
+                                                               int64_t* __restrict__ ids,
+                                                               float* __restrict__ scratch,
+                                                               int64_t scratch_stride) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[32];
   __shared__ int cnt_s[32];
   const T* row = logits + (size_t)blockIdx.x * stride;
+  float* pr = scratch + (size_t)blockIdx.x * scratch_stride;
+  const int groups = (vocab + 3) / 4;
 
   // softmax(logits.float() / temperature) in fp32.
   float mx = -INFINITY;
@@ -159,19 +169,34 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
   float se = 0.f;
   for (int i = threadIdx.x; i < vocab; i += blockDim.x) se += expf(scaled<T>(row, i, temperature) - mx);
   se = block_reduce_sum(se, red);
-  auto prob = [&](int i) { return expf(scaled<T>(row, i, temperature) - mx) / se; };
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    float4 q;
+    float* qq = &q.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * g + e;
+      qq[e] = i < vocab ? expf(scaled<T>(row, i, temperature) - mx) / se : -1.f;  // -1: past the row
+    }
+    reinterpret_cast<float4*>(pr)[g] = q;
+  }
 
   auto mass_gt = [&](float v) {
     float acc = 0.f;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-      const float p = prob(i);
-      if (p > v) acc += p;
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+      const float4 q = reinterpret_cast<const float4*>(pr)[g];
+      if (q.x > v) acc += q.x;
+      if (q.y > v) acc += q.y;
+      if (q.z > v) acc += q.z;
+      if (q.w > v) acc += q.w;
     }
     return block_reduce_sum(acc, red);
   };
   auto count_eq = [&](float v) {
     int c = 0;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) c += prob(i) == v;
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+      const float4 q = reinterpret_cast<const float4*>(pr)[g];
+      c += (q.x == v) + (q.y == v) + (q.z == v) + (q.w == v);
+    }
     c = __reduce_add_sync(0xffffffffu, c);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __syncthreads();
@@ -180,9 +205,12 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
     int t = lane < (int)(blockDim.x >> 5) ? cnt_s[lane] : 0;
     return __reduce_add_sync(0xffffffffu, t);
   };
-  // Smallest non-negative float v (by bit pattern) with mass_gt(v) <= target.
-  auto search = [&](float target) {
-    uint32_t lo = 0u, hi = __float_as_uint(1.0f);
+  // Smallest non-negative float v (by bit pattern) with mass_gt(v) <= target;
+  // every v at or above the largest probability qualifies.  (A 32-way search
+  // with per-thread buckets in shared memory was measured slower: each pass
+  // then costs more than the passes it saves.)
+  auto search = [&](float target, uint32_t hi) {
+    uint32_t lo = 0u;
     while (lo < hi) {
       const uint32_t mid = lo + (hi - lo) / 2;
       if (mass_gt(__uint_as_float(mid)) <= target) hi = mid;
@@ -190,9 +218,10 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
     }
     return __uint_as_float(lo);
   };
+  const uint32_t top = __float_as_uint(1.0f / se);  // the largest probability, exp(0) / se
 
   // (1) The kept prefix.
-  const float bstar = search(top_p);
+  const float bstar = search(top_p, top);
   const float gt_b = mass_gt(bstar);
   const int cnt_b = count_eq(bstar);
   int keep_b = cnt_b;
@@ -204,7 +233,7 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
 
   // (2) The drawn level and the rank inside its tie group.
   const float x = uniforms[blockIdx.x] * z;
-  const float w = search(x);
+  const float w = search(x, top);
   const float gt_w = mass_gt(w);
   const int cnt_w = count_eq(w);
   int limit = (w == bstar) ? keep_b : cnt_w;
@@ -212,34 +241,42 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
   int rank = w > 0.f ? (int)floorf((x - gt_w) / w) : 0;
   rank = max(0, min(rank, limit - 1));
 
-  // (3) The token holding that rank among the indices with p == w.
-  __shared__ int found;
-  __shared__ int base_count;
-  if (threadIdx.x == 0) {
-    found = -1;
-    base_count = 0;
+  // (3) The token holding that rank among the indices with p == w: thread t
+  // counts its contiguous run of indices, an exclusive scan over threads
+  // finds the run holding the rank, and that thread walks its run.
+  __syncthreads();  // every probability written above is visible to the block
+  const int run = (vocab + blockDim.x - 1) / blockDim.x;
+  const int i0 = threadIdx.x * run, i1 = min(vocab, i0 + run);
+  int mine = 0;
+  for (int i = i0; i < i1; ++i) mine += pr[i] == w;
+  // exclusive scan of `mine` over the block
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
   __syncthreads();
-  for (int t0 = 0; t0 < vocab; t0 += blockDim.x) {
-    const int i = t0 + threadIdx.x;
-    const bool hit = i < vocab && prob(i) == w;
-    const unsigned bal = __ballot_sync(0xffffffffu, hit);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) cnt_s[warp] = __popc(bal);
-    __syncthreads();
-    int before = base_count;
-    for (int k = 0; k < warp; ++k) before += cnt_s[k];
-    before += __popc(bal & ((1u << lane) - 1u));
-    if (hit && before == rank) found = i;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int tot = 0;
-      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += cnt_s[k];
-      base_count += tot;
-    }
-    __syncthreads();
-    if (found >= 0) break;
+  if (lane == 31) cnt_s[warp] = incl;
+  __syncthreads();
+  int before = incl - mine;
+  for (int k = 0; k < warp; ++k) before += cnt_s[k];
+  __shared__ int found;
+  if (threadIdx.x == 0) found = -1;
+  __syncthreads();
+  if (mine > 0 && rank >= before && rank < before + mine) {
+    int k = before;
+    for (int i = i0; i < i1; ++i)
+      if (pr[i] == w) {
+        if (k == rank) {
+          found = i;
+          break;
+        }
+        ++k;
+      }
   }
+  __syncthreads();
   if (threadIdx.x == 0) ids[blockIdx.x] = found >= 0 ? found : 0;
 }
 
@@ -261,12 +298,32 @@ cudaError_t launch_top_p(int dtype, const void* logits, int rows, int vocab, int
                          cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   if (!(temperature > 0.f)) return launch_argmax(dtype, logits, rows, vocab, stride, ids, s);
+  // The rows' probabilities: a per-device scratch buffer, grown on demand
+  // (the growth synchronises the device once).
+  static float* scratch[64] = {};
+  static size_t scratch_elems[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const int64_t pstride = ((int64_t)vocab + 3) / 4 * 4;
+  const size_t need = (size_t)rows * (size_t)pstride;
+  if (need > scratch_elems[dev]) {
+    if (scratch[dev]) {
+      cudaDeviceSynchronize();
+      cudaFree(scratch[dev]);
+      scratch[dev] = nullptr;
+      scratch_elems[dev] = 0;
+    }
+    const cudaError_t e = cudaMalloc(&scratch[dev], need * sizeof(float));
+    if (e != cudaSuccess) return e;
+    scratch_elems[dev] = need;
+  }
   if (dtype == kBF16)
-    { const cudaError_t _le = launch_pdl(top_p_kernel<__nv_bfloat16>, dim3(rows), dim3(kSampleThreads), 0, s, 
-        (const __nv_bfloat16*)logits, vocab, stride, temperature, top_p, uniforms, ids); if (_le != cudaSuccess) return _le; }
+    { const cudaError_t _le = launch_pdl(top_p_kernel<__nv_bfloat16>, dim3(rows), dim3(kSampleThreads), 0, s,
+        (const __nv_bfloat16*)logits, vocab, stride, temperature, top_p, uniforms, ids, scratch[dev], pstride); if (_le != cudaSuccess) return _le; }
   else
     { const cudaError_t _le = launch_pdl(top_p_kernel<float>, dim3(rows), dim3(kSampleThreads), 0, s, (const float*)logits, vocab, stride,
-                                                        temperature, top_p, uniforms, ids); if (_le != cudaSuccess) return _le; }
+                                                        temperature, top_p, uniforms, ids, scratch[dev], pstride); if (_le != cudaSuccess) return _le; }
   return cudaGetLastError();
 }
 

@@ -120,8 +120,11 @@ def decode_loop(
 # ---------------------------------------------------------------------------
 
 def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[float, float, str],
-                       traffic: dict | None = None) -> None:
+                       traffic: dict | None = None, top_p: tuple[float, float] | None = None) -> None:
+    """``top_p`` = (temperature, p): the last stage samples with a seeded device
+    generator instead of selecting greedily inside its lm_head."""
     from gpu_mesh_b200 import greedy_sample
+    from gpu_mesh_b200.sampling import top_p_sample
     from gpu_mesh_b200.config import split_layers
     from gpu_mesh_b200.stage import B200Stage
     from gpu_mesh_b200.weights import synthetic_stage_state
@@ -167,9 +170,11 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 return stage.forward_slot(slots[grp], None, input_ids=x, logits="last", check_values=False)
             return stage.forward_slot(slots[grp], x, logits="last", check_values=False)
 
+        sample_gen = torch.Generator(device=dev).manual_seed(1234)
+
         def decode_on(slot_ids, x):
             # the last stage selects the greedy tokens inside its lm_head
-            if ring.last:
+            if ring.last and top_p is None:
                 return stage.decode_greedy(slot_ids, None if ring.first else x,
                                            input_ids=x if ring.first else None)[0]
             if ring.first:
@@ -182,6 +187,8 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
         def tokens_of(out):
             if out.dtype == torch.int64:  # already selected by decode_greedy
                 return out.view(-1, 1)
+            if top_p is not None:
+                return top_p_sample(out[:, -1], *top_p, generator=sample_gen).unsqueeze(-1)
             return greedy_sample(out[:, -1]).unsqueeze(-1)
 
         def sample(k, grp, out):
