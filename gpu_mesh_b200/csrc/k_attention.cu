@@ -286,8 +286,6 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   if (a.use_tc && attention_prefill_tc_applicable(a.dtype, a.D, a.nq / a.nkv, a.S))
     return launch_attention_prefill_tc(a, s);  // query tiles on tcgen05, scores and output in TMEM
-  if (a.use_tc && attention_prefill_applicable(a.dtype, a.D, a.nq / a.nkv, a.S))
-    return launch_attention_prefill(a, s);  // query tiles on mma.sync
   if (a.use_tc && attention_tc_applicable(a.dtype, a.D, a.nq / a.nkv))
     return launch_attention_tc(a, splits, s);  // merges its chunks itself
   dim3 grid(M, a.nkv, splits);

@@ -244,12 +244,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 // `out` itself (no combine launch); its fp32 scratch need is
 // attention_tc_scratch_elems, its counters one per (token, KV head).
 bool attention_tc_applicable(int dtype, int D, int G);
-// Prefill / multi-token attention with query tiles (k_attention_prefill.cu):
-// bf16, head_dim 64 or 128, G dividing 16, S >= 8 query tokens per row.
-bool attention_prefill_applicable(int dtype, int D, int G, int S);
-cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t s);
-// The same work on tcgen05 (k_attention_prefill_tc.cu): scores and output in
-// TMEM, one softmax thread per query row.
+// Prefill / multi-token attention with query tiles on tcgen05
+// (k_attention_prefill_tc.cu): bf16, head_dim 64 or 128, G dividing 16,
+// S >= 8 query tokens per row; scores and output in TMEM.
 bool attention_prefill_tc_applicable(int dtype, int D, int G, int S);
 cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s);
 size_t attention_tc_scratch_elems(int nq, int D);
