@@ -71,6 +71,75 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __r
   }
 }
 
+// 16 bytes of rounded floats to T (8 bf16 or 4 fp32) in one store.
+template <typename T>
+__device__ __forceinline__ void store16_f(T* p, const float* v) {
+  if constexpr (sizeof(T) == 2) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i])) |
+             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1])) << 16);
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// RMSNorm of many rows (prefill): one warp per row, 8 rows per CTA.  Lane l
+// keeps the partial sums of the 16 threads l, 32 + l, ..., 480 + l of the
+// 512-thread kernel (same vectors, same order), reduces each over the warp,
+// then reduces the 16 warp sums as the block reduction does, so every output
+// is bit-identical to rmsnorm_kernel's.
+constexpr int kRowsPerCta = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kRowsPerCta * 32) rmsnorm_rows_kernel(const T* __restrict__ x, int64_t xs,
+                                                                        const T* __restrict__ w, int H, float eps,
+                                                                        T* __restrict__ y, int M) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int kVirt = kNormThreads / 32;  // warps of the block-per-row kernel
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const T* xr = x + (size_t)m * xs;
+  T* yr = y + (size_t)m * H;
+  constexpr int VEC = Vec16<T>::N;
+  const int nv = H / VEC;
+  float part[kVirt];
+#pragma unroll
+  for (int v = 0; v < kVirt; ++v) part[v] = 0.f;
+  for (int base = 0; base < nv; base += kNormThreads) {
+#pragma unroll
+    for (int v = 0; v < kVirt; ++v) {
+      const int i = base + v * 32 + lane;
+      if (i < nv) {
+        float e[VEC];
+        load16_f<T>(xr + i * VEC, e);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) part[v] += e[j] * e[j];
+      }
+    }
+  }
+  float t = 0.f;
+#pragma unroll
+  for (int v = 0; v < kVirt; ++v) {
+    const float sv = warp_sum(part[v]);
+    if (lane == v) t = sv;
+  }
+  const float ss = warp_sum(t);
+  const float r = 1.0f / sqrtf(ss / (float)H + eps);
+  for (int i = lane; i < nv; i += 32) {
+    float e[VEC], g[VEC], o[VEC];
+    load16_f<T>(xr + i * VEC, e);
+    load16_f<T>(w + i * VEC, g);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) o[j] = rt<T>(rt<T>(e[j] * r) * g[j]);
+    store16_f<T>(yr + i * VEC, o);
+  }
+}
+
 // The residual epilogue of a decode GEMM left as pieces, then (optionally)
 // the RMSNorm of the new residual row, in the RMSNorm reduction order (one
 // 8-element vector per thread at H <= 4096, so every piece load of the row
@@ -152,6 +221,17 @@ cudaError_t launch_rmsnorm(int dtype, const void* x, int64_t xs, const void* w, 
                            float eps, void* y, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   const int threads = kNormThreads;
+  if (M > kRowsPerCta * 4) {  // many rows: a warp per row (same results)
+    const dim3 grid((M + kRowsPerCta - 1) / kRowsPerCta);
+    const cudaError_t e =
+        dtype == kBF16
+            ? launch_pdl(rmsnorm_rows_kernel<__nv_bfloat16>, grid, dim3(kRowsPerCta * 32), 0, s,
+                         (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y, M)
+            : launch_pdl(rmsnorm_rows_kernel<float>, grid, dim3(kRowsPerCta * 32), 0, s, (const float*)x, xs,
+                         (const float*)w, H, eps, (float*)y, M);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
   if (dtype == kBF16)
     { const cudaError_t _le = launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(threads), 0, s, 
         (const __nv_bfloat16*)x, xs, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)y); if (_le != cudaSuccess) return _le; }
