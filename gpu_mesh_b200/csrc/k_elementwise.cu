@@ -71,21 +71,6 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __r
   }
 }
 
-// 16 bytes of rounded floats to T (8 bf16 or 4 fp32) in one store.
-template <typename T>
-__device__ __forceinline__ void store16_f(T* p, const float* v) {
-  if constexpr (sizeof(T) == 2) {
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i])) |
-             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1])) << 16);
-    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-  } else {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-  }
-}
-
 // RMSNorm of many rows (prefill): one warp per row, 8 rows per CTA.  Lane l
 // keeps the partial sums of the 16 threads l, 32 + l, ..., 480 + l of the
 // 512-thread kernel (same vectors, same order), reduces each over the warp,

@@ -87,118 +87,211 @@ __global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_kernel(QkvPostArgs
   }
 }
 
-// VEC-wide loads and stores (VEC consecutive elements, 4 to 16 bytes).
-template <typename T, int VEC>
-__device__ __forceinline__ void load_vec(const T* p, float* out) {
-  if constexpr (sizeof(T) == 2 && VEC == 4) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
-    out[0] = __uint_as_float(v.x << 16); out[1] = __uint_as_float(v.x & 0xffff0000u);
-    out[2] = __uint_as_float(v.y << 16); out[3] = __uint_as_float(v.y & 0xffff0000u);
-  } else if constexpr (sizeof(T) == 2 && VEC == 2) {
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
-    out[0] = __uint_as_float(v << 16); out[1] = __uint_as_float(v & 0xffff0000u);
-  } else if constexpr (VEC == 4) {
-    const float4 v = *reinterpret_cast<const float4*>(p);
-    out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
-  } else {
-    const float2 v = *reinterpret_cast<const float2*>(p);
-    out[0] = v.x; out[1] = v.y;
+// Decode rows (bf16, head_dim 64 or 128) from the qkv projection's pieces,
+// 16 bytes per lane: VEC = 8 consecutive dims, LPH = D / VEC lanes per head,
+// so a warp takes HPW = 32 / LPH heads of one token (a group) at once and
+// the rotate-half partner (dims d ± D/2) sits LPH / 2 lanes away.  Warps
+// stride over the (token, group) units; each lane sums its dims' pieces
+// straight into registers.
+constexpr int kVecWarps = 8;
+
+// Streaming multiprocessors of the current device (cached per device).
+inline int sm_count_cached() {
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
   }
+  return n[dev];
 }
 
-template <typename T, int VEC>
-__device__ __forceinline__ void store_vec(T* p, const float* in) {
-  if constexpr (sizeof(T) == 2) {
-    uint32_t w[VEC / 2];
-#pragma unroll
-    for (int i = 0; i < VEC / 2; ++i)
-      w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(in[2 * i])) |
-             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(in[2 * i + 1])) << 16);
-    if constexpr (VEC == 4) *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
-    else *reinterpret_cast<uint32_t*>(p) = w[0];
-  } else {
-    if constexpr (VEC == 4) *reinterpret_cast<float4*>(p) = make_float4(in[0], in[1], in[2], in[3]);
-    else *reinterpret_cast<float2*>(p) = make_float2(in[0], in[1]);
-  }
-}
-
-// The same work with one warp per head and VEC = D / 32 consecutive dims per
-// lane (head_dim 64 or 128): vector loads and stores, the rotate-half
-// partner (dims d ± D/2) from lane ^ 16 by a shuffle.
-template <typename T, int VEC>
-__global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_vec_kernel(QkvPostArgs a) {
+template <typename T, int D>
+__global__ void __launch_bounds__(kVecWarps * 32) qkv_post_pieces_kernel(QkvPostArgs a) {
   pdl_trigger();
   pdl_wait();
-  constexpr int D = VEC * 32, half = D / 2;
-  __shared__ float xs[kHeadsPerCta][D];
+  constexpr int VEC = 16 / sizeof(T), LPH = D / VEC, HPW = 32 / LPH, half = D / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x;
-  const int hh = blockIdx.y * kHeadsPerCta + warp;
+  const int sub = lane / LPH, hl = lane % LPH;
+  const int d0 = hl * VEC, dh = d0 % half;
+  const bool lower = d0 < half;
   const int nh = a.nq + 2 * a.nkv;
-  if (hh >= nh) return;
-  const int b = m / a.S, s = m % a.S;
-  const RowDesc rd = a.rows[b];
-  const int cache_pos = rd.past + s;
-  int64_t pos = a.positions ? a.positions[m] : (int64_t)cache_pos;
-  if (pos < 0 || pos >= a.max_pos) {
-    flag_error(a.err, kErrPositionRange);
-    pos = pos < 0 ? 0 : a.max_pos - 1;
-  }
-  const int d0 = lane * VEC;
-  float x[VEC];
-  if (a.use_pieces) {  // the projection's pieces, rounded as its store epilogue would
-    float* xw = xs[warp];
-    for (int d = lane * 4; d < D; d += 128) {
-      float acc[4];
-      pieces_sum4(a.pieces, m, hh * D + d, acc);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) xw[d + i] = rt<T>(acc[i]);
+  const int groups = (nh + HPW - 1) / HPW;
+  const long long units = (long long)a.B * a.S * groups;
+  for (long long u = (long long)blockIdx.x * kVecWarps + warp; u < units; u += (long long)gridDim.x * kVecWarps) {
+    const int m = (int)(u / groups);
+    const int hh = (int)(u % groups) * HPW + sub;
+    const bool valid = hh < nh;  // lanes past the last head still join the shuffles
+    const int b = m / a.S, s = m % a.S;
+    const RowDesc rd = a.rows[b];
+    const int cache_pos = rd.past + s;
+    int64_t pos = a.positions ? a.positions[m] : (int64_t)cache_pos;
+    if (pos < 0 || pos >= a.max_pos) {
+      if (valid && hl == 0) flag_error(a.err, kErrPositionRange);
+      pos = pos < 0 ? 0 : a.max_pos - 1;
     }
-    __syncwarp();
+    float x[VEC];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) x[i] = xw[d0 + i];
-  } else {
-    load_vec<T, VEC>((const T*)a.qkv + (size_t)m * nh * D + (size_t)hh * D + d0, x);
+    for (int i = 0; i < VEC; ++i) x[i] = 0.f;
+    if (valid) {
+      // the projection's pieces, rounded as its store epilogue would
+      if constexpr (VEC == 8) {
+        pieces_sum8(a.pieces, m, hh * D + d0, x);
+      } else {
+        pieces_sum4(a.pieces, m, hh * D + d0, x);
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = rt<T>(x[i]);
+    }
+    const bool is_q = hh < a.nq;
+    const bool is_k = !is_q && hh < a.nq + a.nkv;
+    const bool is_v = valid && !is_q && !is_k;
+    T* kv = (T*)rd.kv_base;
+    const T* nw = is_q ? (const T*)a.q_norm : (const T*)a.k_norm;
+    // QK-norm: a head's LPH lanes reduce among themselves (every lane runs
+    // the shuffles; only Q / K lanes of a model with the norm use the sum).
+    if (a.q_norm || a.k_norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) ss += x[i] * x[i];
+#pragma unroll
+      for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (valid && !is_v && nw) {
+        const float r = 1.0f / sqrtf(ss / (float)D + a.eps);
+        float g[VEC];
+        load16_f<T>(nw + d0, g);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) x[i] = rt<T>(rt<T>(x[i] * r) * g[i]);
+      }
+    }
+    float c[VEC], sv[VEC], y[VEC];
+    load16_f<T>((const T*)a.cos + (size_t)pos * half + dh, c);
+    load16_f<T>((const T*)a.sin + (size_t)pos * half + dh, sv);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[i], LPH / 2);
+      const float rot = lower ? -partner : partner;
+      y[i] = rt<T>(x[i] * c[i]) + rt<T>(rot * sv[i]);
+    }
+    if (!valid) continue;
+    if (is_v) {  // value head: plain append
+      store16_f<T>(kv + kv_offset_elems(a.layer, 1, rd.slot_rows, rd.row, a.nkv, hh - a.nq - a.nkv, rd.cap, D,
+                                        cache_pos) + d0,
+                   x);
+    } else if (is_q) {
+      store16_f<T>((T*)a.q_out + ((size_t)m * a.nq + hh) * D + d0, y);
+    } else {
+      store16_f<T>(kv + kv_offset_elems(a.layer, 0, rd.slot_rows, rd.row, a.nkv, hh - a.nq, rd.cap, D, cache_pos) +
+                       d0,
+                   y);
+    }
   }
+}
 
-  const bool is_q = hh < a.nq;
-  const bool is_k = !is_q && hh < a.nq + a.nkv;
-  T* kv = (T*)rd.kv_base;
-  if (!is_q && !is_k) {  // value head: plain append
-    const int h = hh - a.nq - a.nkv;
-    store_vec<T, VEC>(kv + kv_offset_elems(a.layer, 1, rd.slot_rows, rd.row, a.nkv, h, rd.cap, D, cache_pos) + d0, x);
-    return;
-  }
-  const T* nw = is_q ? (const T*)a.q_norm : (const T*)a.k_norm;
-  if (nw) {
-    float ss = 0.f;
+// Many tokens (prefill): one CTA per token at a time.  The 256 threads take
+// the token's qkv row as 16-byte vectors (thread i holds vectors i, i + 256,
+// ..., up to kRowVecs of them, all loaded before any arithmetic), so the
+// row, the row descriptor and the token's cos / sin are read once and in
+// parallel; a head's LPH lanes stay inside one warp, so the QK-norm sum and
+// the rotate-half partner are shuffles as above.
+constexpr int kRowThreads = 256;
+constexpr int kRowVecs = 4;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kRowThreads) qkv_post_rows_kernel(QkvPostArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int VEC = 16 / sizeof(T), LPH = D / VEC, half = D / 2;
+  static_assert(kRowThreads % LPH == 0, "a head's lanes must not straddle threads of different rounds");
+  const int t = threadIdx.x;
+  const int hl = t % LPH;
+  const int d0 = hl * VEC, dh = d0 % half;
+  const bool lower = d0 < half;
+  const int nh = a.nq + 2 * a.nkv;
+  const int vecs = nh * LPH;  // 16-byte vectors in a token's qkv row
+  const int M = a.B * a.S;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    const T* row = (const T*)a.qkv + (size_t)m * nh * D;
+    const int b = m / a.S, s = m % a.S;
+    for (int v0 = 0; v0 < vecs; v0 += kRowVecs * kRowThreads) {
+      float x[kRowVecs][VEC];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) ss += x[i] * x[i];
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss / (float)D + a.eps);
-    float g[VEC];
-    load_vec<T, VEC>(nw + d0, g);
+      for (int j = 0; j < kRowVecs; ++j) {
+        const int v = v0 + j * kRowThreads + t;
+        if (v < vecs) {
+          load16_f<T>(row + (size_t)v * VEC, x[j]);
+        } else {
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) x[i] = rt<T>(rt<T>(x[i] * r) * g[i]);
-  }
-  float c[VEC], sv[VEC], y[VEC];
-  const int dh = (lane & 15) * VEC;  // d0 % half
-  load_vec<T, VEC>((const T*)a.cos + (size_t)pos * half + dh, c);
-  load_vec<T, VEC>((const T*)a.sin + (size_t)pos * half + dh, sv);
+          for (int i = 0; i < VEC; ++i) x[j][i] = 0.f;
+        }
+      }
+      const RowDesc rd = a.rows[b];
+      const int cache_pos = rd.past + s;
+      int64_t pos = a.positions ? a.positions[m] : (int64_t)cache_pos;
+      if (pos < 0 || pos >= a.max_pos) {
+        if (t == 0 && v0 == 0) flag_error(a.err, kErrPositionRange);
+        pos = pos < 0 ? 0 : a.max_pos - 1;
+      }
+      float c[VEC], sv[VEC];
+      load16_f<T>((const T*)a.cos + (size_t)pos * half + dh, c);
+      load16_f<T>((const T*)a.sin + (size_t)pos * half + dh, sv);
+      T* kv = (T*)rd.kv_base;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
-    const float rot = lane < 16 ? -partner : partner;
-    y[i] = rt<T>(x[i] * c[i]) + rt<T>(rot * sv[i]);
+      for (int j = 0; j < kRowVecs; ++j) {
+        const int v = v0 + j * kRowThreads + t;
+        if (v0 + j * kRowThreads >= vecs) break;  // uniform over the CTA
+        const bool valid = v < vecs;
+        const int hh = v / LPH;
+        const bool is_q = hh < a.nq;
+        const bool is_k = !is_q && hh < a.nq + a.nkv;
+        const bool is_v = valid && !is_q && !is_k;
+        const T* nw = is_q ? (const T*)a.q_norm : (const T*)a.k_norm;
+        if (a.q_norm || a.k_norm) {
+          float ss = 0.f;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) ss += x[j][i] * x[j][i];
+#pragma unroll
+          for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (valid && !is_v && nw) {
+            const float r = 1.0f / sqrtf(ss / (float)D + a.eps);
+            float g[VEC];
+            load16_f<T>(nw + d0, g);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) x[j][i] = rt<T>(rt<T>(x[j][i] * r) * g[i]);
+          }
+        }
+        float y[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float partner = __shfl_xor_sync(0xffffffffu, x[j][i], LPH / 2);
+          const float rot = lower ? -partner : partner;
+          y[i] = rt<T>(x[j][i] * c[i]) + rt<T>(rot * sv[i]);
+        }
+        if (!valid) continue;
+        if (is_v) {  // value head: plain append
+          store16_f<T>(kv + kv_offset_elems(a.layer, 1, rd.slot_rows, rd.row, a.nkv, hh - a.nq - a.nkv, rd.cap, D,
+                                            cache_pos) + d0,
+                       x[j]);
+        } else if (is_q) {
+          store16_f<T>((T*)a.q_out + ((size_t)m * a.nq + hh) * D + d0, y);
+        } else {
+          store16_f<T>(kv + kv_offset_elems(a.layer, 0, rd.slot_rows, rd.row, a.nkv, hh - a.nq, rd.cap, D,
+                                            cache_pos) + d0,
+                       y);
+        }
+      }
+    }
   }
-  T* dst;
-  if (is_q) {
-    dst = (T*)a.q_out + ((size_t)m * a.nq + hh) * D;
-  } else {
-    const int h = hh - a.nq;
-    dst = kv + kv_offset_elems(a.layer, 0, rd.slot_rows, rd.row, a.nkv, h, rd.cap, D, cache_pos);
-  }
-  store_vec<T, VEC>(dst + d0, y);
+}
+
+// Resident CTAs per SM of a kernel at `threads` threads.
+inline int resident_ctas(void (*kernel)(QkvPostArgs), int threads) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n < 1) n = 1;
+  return n;
 }
 
 }  // namespace
@@ -206,22 +299,32 @@ __global__ void __launch_bounds__(kHeadsPerCta * 32) qkv_post_vec_kernel(QkvPost
 cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
   const int M = a.B * a.S;
   if (M == 0) return cudaSuccess;
-  dim3 grid(M, (a.nq + 2 * a.nkv + kHeadsPerCta - 1) / kHeadsPerCta);
-  if (a.D == 128 || a.D == 64) {
-    cudaError_t e;
+  cudaError_t e;
+  const bool vec = a.D == 128 || a.D == 64;
+  if (vec && a.use_pieces && a.dtype == kBF16) {  // decode rows: a warp per (token, head group)
+    const int hpw = 32 / (a.D * 2 / 16);
+    const long long units = (long long)M * ((a.nq + 2 * a.nkv + hpw - 1) / hpw);
+    long long blocks = (units + kVecWarps - 1) / kVecWarps;
+    const long long cap = 8LL * sm_count_cached();
+    if (blocks > cap) blocks = cap;
+    e = launch_pdl(a.D == 128 ? qkv_post_pieces_kernel<__nv_bfloat16, 128>
+                              : qkv_post_pieces_kernel<__nv_bfloat16, 64>,
+                   dim3((unsigned)blocks), dim3(kVecWarps * 32), 0, s, a);
+  } else if (vec && !a.use_pieces) {  // a CTA per token
+    void (*k)(QkvPostArgs);
     if (a.dtype == kBF16)
-      e = a.D == 128 ? launch_pdl(qkv_post_vec_kernel<__nv_bfloat16, 4>, grid, dim3(kHeadsPerCta * 32), 0, s, a)
-                     : launch_pdl(qkv_post_vec_kernel<__nv_bfloat16, 2>, grid, dim3(kHeadsPerCta * 32), 0, s, a);
+      k = a.D == 128 ? qkv_post_rows_kernel<__nv_bfloat16, 128> : qkv_post_rows_kernel<__nv_bfloat16, 64>;
     else
-      e = a.D == 128 ? launch_pdl(qkv_post_vec_kernel<float, 4>, grid, dim3(kHeadsPerCta * 32), 0, s, a)
-                     : launch_pdl(qkv_post_vec_kernel<float, 2>, grid, dim3(kHeadsPerCta * 32), 0, s, a);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
+      k = a.D == 128 ? qkv_post_rows_kernel<float, 128> : qkv_post_rows_kernel<float, 64>;
+    const long long cap = (long long)resident_ctas(k, kRowThreads) * sm_count_cached();
+    const unsigned blocks = (unsigned)(M < cap ? M : cap);
+    e = launch_pdl(k, dim3(blocks), dim3(kRowThreads), 0, s, a);
+  } else {
+    const dim3 grid(M, (a.nq + 2 * a.nkv + kHeadsPerCta - 1) / kHeadsPerCta), block(kHeadsPerCta * 32);
+    e = a.dtype == kBF16 ? launch_pdl(qkv_post_kernel<__nv_bfloat16>, grid, block, 0, s, a)
+                         : launch_pdl(qkv_post_kernel<float>, grid, block, 0, s, a);
   }
-  if (a.dtype == kBF16)
-    { const cudaError_t _le = launch_pdl(qkv_post_kernel<__nv_bfloat16>, dim3(grid), dim3(kHeadsPerCta * 32), 0, s, a); if (_le != cudaSuccess) return _le; }
-  else
-    { const cudaError_t _le = launch_pdl(qkv_post_kernel<float>, dim3(grid), dim3(kHeadsPerCta * 32), 0, s, a); if (_le != cudaSuccess) return _le; }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

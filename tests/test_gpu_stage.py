@@ -303,3 +303,50 @@ def test_attention_over_imported_cache_matches_oracle(D, nq, nkv, T):
         ex = exact.forward(input_ids=ids, key="c").float()
     _exact_bar(got, ref, ex, f"T={T}")
     stage.close()
+
+
+# RoPE / QK-norm / KV append kernels (every variant) against the oracle
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize(
+    "dtype,D,nq,nkv,qk_norm",
+    [
+        (torch.float32, 128, 4, 2, True),    # a CTA per token, 32 lanes per head
+        (torch.float32, 64, 8, 2, False),    # 16 lanes per head
+        (torch.bfloat16, 128, 12, 4, True),  # 16 lanes per head, two rounds of the row
+        (torch.bfloat16, 64, 5, 1, False),   # 8 lanes per head, 7 heads: partial warps and groups
+        (torch.bfloat16, 32, 4, 2, False),   # head_dim outside the vector kernels
+    ],
+    ids=["f32-d128-qkn", "f32-d64", "bf16-d128-qkn", "bf16-d64-odd", "bf16-d32"],
+)
+def test_rope_kv_append_matches_oracle(dtype, D, nq, nkv, qk_norm):
+    """Prefill of 2 x 40 tokens (the many-token kernel) then two decode
+    steps (the decode-row kernel, reading the projection's pieces in bf16):
+    the exported K / V cache and the logits against the oracle.  Cache bar:
+    max |cuda - oracle| <= 1e-4 (fp32) or 2e-2 (bf16) x max |oracle|."""
+    cfg = LlamaConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=nq, num_key_value_heads=nkv, head_dim=D,
+                      max_position_embeddings=512, rope_theta=500000.0,
+                      **({"qk_norm": True, "mask_policy": "cache"} if qk_norm else {}))
+    full = synthetic_model_state(cfg, seed=21, dtype=dtype)
+    stage = B200Stage(cfg, 0, 2, has_embedding=True, has_lm_head=True, device=DEV, dtype=dtype, state_dict=full)
+    oracle = R.OracleStage(cfg, 0, 2, True, True, full, dtype)
+    rel = 1e-4 if dtype == torch.float32 else 2e-2
+    g = torch.Generator().manual_seed(D + nq)
+    stage.kv_reserve(1, 2, 64)
+    ids = torch.randint(0, cfg.vocab_size, (2, 40), generator=g)
+    steps = [ids] + [torch.randint(0, cfg.vocab_size, (2, 1), generator=g) for _ in range(2)]
+    for i, x in enumerate(steps):
+        got = stage.forward_slot(1, None, input_ids=x).float().cpu()
+        ref = oracle.forward(input_ids=x, key="c").float()
+        assert (got - ref).abs().max() <= tol_logits(dtype, ref), i
+        for layer, ((gk, gv), (rk, rv)) in enumerate(zip(stage.kv_export(1), oracle.caches["c"])):
+            for name, a, b in (("k", gk, rk), ("v", gv, rv)):
+                b = b.float()
+                err = float((a.float().cpu() - b).abs().max())
+                assert err <= rel * float(b.abs().max()), (i, layer, name, err)
+    stage.close()
+
+
+def tol_logits(dtype, ref: torch.Tensor) -> float:
+    return 1e-4 * float(ref.abs().max()) if dtype == torch.float32 else 2e-2
