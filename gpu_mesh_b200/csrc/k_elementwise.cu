@@ -133,6 +133,12 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_pieces_kernel(Pieces 
                                                                 const __nv_bfloat16* __restrict__ w, int H,
                                                                 float eps, __nv_bfloat16* __restrict__ y) {
   pdl_trigger();
+  // The norm weights do not depend on the kernels before this one: at
+  // H <= 8 * blockDim.x each thread's one vector of them is requested before
+  // the wait.
+  const bool one = w && H / 8 <= (int)blockDim.x;
+  float g0[8];
+  if (one && (int)threadIdx.x < H / 8) load16_f<__nv_bfloat16>(w + threadIdx.x * 8, g0);
   pdl_wait();
   __shared__ float red[32];
   const int m = blockIdx.x;
@@ -156,12 +162,17 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_pieces_kernel(Pieces 
   const float r = 1.0f / sqrtf(ss / (float)H + eps);
   __nv_bfloat16* yr = y + (size_t)m * H;
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
-    float v[8], g[8];
+    float v[8], g[8], o[8];
     load16_f<__nv_bfloat16>(xr + i * 8, v);  // this thread's own stores
-    load16_f<__nv_bfloat16>(w + i * 8, g);
+    if (one) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      stf<__nv_bfloat16>(yr + i * 8 + j, rt<__nv_bfloat16>(rt<__nv_bfloat16>(v[j] * r) * g[j]));
+      for (int j = 0; j < 8; ++j) g[j] = g0[j];
+    } else {
+      load16_f<__nv_bfloat16>(w + i * 8, g);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = rt<__nv_bfloat16>(rt<__nv_bfloat16>(v[j] * r) * g[j]);
+    store16_f<__nv_bfloat16>(yr + i * 8, o);
   }
 }
 

@@ -91,6 +91,15 @@ def test_linear_bf16_matches_fp32_reference(M, N, K, epilogue):
     check(y, ref, torch.bfloat16, {"store": 1, "resid": 2, "swiglu": 3}[epilogue])
 
 
+@pytest.mark.parametrize("M,N,K", [(33, 4096, 4096), (300, 688, 256), (1500, 2000, 512), (2048, 4096, 4096)])
+@pytest.mark.parametrize("epilogue", ["store", "resid", "swiglu"])
+def test_linear_single_sm_kernel_matches_fp32_reference(M, N, K, epilogue, monkeypatch):
+    """The single-SM persistent GEMM that stands in where a device cannot
+    co-schedule CTA pairs (selected here by its environment switch)."""
+    monkeypatch.setenv("MESHGPU_GEMM_SINGLE_SM", "1")
+    test_linear_bf16_matches_fp32_reference(M, N, K, epilogue)
+
+
 def test_linear_in_place_residual():
     g = torch.Generator(device=DEV).manual_seed(5)
     x = torch.randn(64, 512, generator=g, device=DEV).to(torch.bfloat16)
