@@ -301,7 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // to both CTAs; each CTA's epilogue drains its own TMEM and arrives on the
 // even CTA's accumulator-free barrier.  No load is multicast.  Every wait is
 // bounded; both CTAs reach the final cluster barrier on every path.
-constexpr int kStagesP = 6;
+#ifndef MG_GEMM_PAIR_STAGES
+#define MG_GEMM_PAIR_STAGES 6
+#endif
+constexpr int kStagesP = MG_GEMM_PAIR_STAGES;
 struct PairSmem {
   static constexpr int kA = 128 * kBK * 2;
   static constexpr int kB = 128 * kBK * 2;
