@@ -292,22 +292,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 // x 256 rows of W (SwiGLU: 128 gate + 128 up rows -> 128 outputs).  CTA r of
 // the pair loads X rows 128r .. 128r + 127 of the tile and W rows
 // 128r .. 128r + 127 (SwiGLU: the gate rows in CTA 0, the up rows in CTA 1)
-// into a 6-stage ring, 32 KB per stage; both CTAs' loads complete on the even
-// CTA's barrier, whose MMA warp issues M = 256 MMAs that read both CTAs'
-// shared memory and leave each CTA's 128 rows x 256 columns in its own TMEM
-// (two accumulators, 512 columns).  Per SM that is 32 KB of operands per
-// 64-deep K block instead of the single-CTA tile's 48 KB for the same MMA
-// work.  Completions (stage free, accumulator ready, all done) are multicast
+// of each 128-deep K block (two 64-column boxes per operand) into a 3-stage
+// ring, 64 KB per stage; both CTAs' loads complete on the even CTA's
+// barrier, whose MMA warp issues eight M = 256 MMAs per stage that read both
+// CTAs' shared memory and leave each CTA's 128 rows x 256 columns in its own
+// TMEM (two accumulators, 512 columns).  Per SM that is 32 KB of operands
+// per 64 of K instead of the single-CTA tile's 48 KB for the same MMA work;
+// 128-deep stages halve the barrier waits and commits per MMA (measured:
+// 0.93-0.97 x cuBLAS against 0.81 with 64-deep stages in a 6-stage ring).  Completions (stage free, accumulator ready, all done) are multicast
 // to both CTAs; each CTA's epilogue drains its own TMEM and arrives on the
 // even CTA's accumulator-free barrier.  No load is multicast.  Every wait is
 // bounded; both CTAs reach the final cluster barrier on every path.
 #ifndef MG_GEMM_PAIR_STAGES
-#define MG_GEMM_PAIR_STAGES 6
+#define MG_GEMM_PAIR_STAGES 3
 #endif
 constexpr int kStagesP = MG_GEMM_PAIR_STAGES;
+#ifndef MG_GEMM_PAIR_SUB
+#define MG_GEMM_PAIR_SUB 2
+#endif
+constexpr int kSubP = MG_GEMM_PAIR_SUB;  // 64-wide K boxes per stage and operand
+constexpr int kBKP = kSubP * kBK;         // K depth of a stage
 struct PairSmem {
-  static constexpr int kA = 128 * kBK * 2;
-  static constexpr int kB = 128 * kBK * 2;
+  static constexpr int kSub = 128 * kBK * 2;  // one 128 x 64 box
+  static constexpr int kA = kSubP * kSub;
+  static constexpr int kB = kSubP * kSub;
   static constexpr int kTiles = kStagesP * (kA + kB);
   static constexpr int kBytes = kTiles + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int nk = (a.K + kBK - 1) / kBK;
+  const int nk = (a.K + kBKP - 1) / kBKP;
   const int ntile = tg.count();
 
   if (threadIdx.x == 0) {
@@ -371,10 +379,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = tg.n(t) * NOUT;
         if (rank == 0) mbar_expect_tx(&full[s], 2 * (L::kA + L::kB));
         const int row = (EPI == kEpiSwiGLU) ? (rank == 0 ? n0 : a.N + n0) : n0 + 128 * (int)rank;
-        tma_load_2d_pair(sb + s * L::kB, &tm_w, full_lead + 8 * s, kb * kBK, row);
+#pragma unroll
+        for (int q = 0; q < kSubP; ++q)
+          tma_load_2d_pair(sb + s * L::kB + q * L::kSub, &tm_w, full_lead + 8 * s, kb * kBKP + q * kBK, row);
       };
       auto load_x = [&](int t, int kb, int s) {
-        tma_load_2d_pair(sa + s * L::kA, &tm_x, full_lead + 8 * s, kb * kBK, tg.m(t) * 256 + 128 * (int)rank);
+#pragma unroll
+        for (int q = 0; q < kSubP; ++q)
+          tma_load_2d_pair(sa + s * L::kA + q * L::kSub, &tm_x, full_lead + 8 * s, kb * kBKP + q * kBK,
+                           tg.m(t) * 256 + 128 * (int)rank);
       };
       long long i = 0;
       const int first = pair;
@@ -422,11 +435,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t da = smem_desc(sa + s * L::kA);
-          const uint64_t db = smem_desc(sb + s * L::kB);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            mma_bf16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int q = 0; q < kSubP; ++q) {
+            const uint64_t da = smem_desc(sa + s * L::kA + q * L::kSub);
+            const uint64_t db = smem_desc(sb + s * L::kB + q * L::kSub);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              mma_bf16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || q > 0 || k > 0) ? 1u : 0u);
+          }
           mma_commit_pair(&empty[s]);
         }
         if (!ok) break;
