@@ -37,6 +37,7 @@ from gpu_mesh_b200.clocks import ClockSampler  # noqa: E402
 METRIC = "decode tok/s (Llama-3-8B arch, 1/2/4/8 B200 stages); attn-decode HBM % of peak"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0  # the same measurement held for seconds under the power cap
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one
 # `ncu --set full` capture of the same kernels on the 2-layer case of this
@@ -103,6 +104,29 @@ def peaks() -> tuple[float, float, str]:
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def sustained_bf16_tflops() -> float:
+    """The measured bf16 GEMM rate held for seconds under the power cap (a
+    prefill is seconds of back-to-back GEMMs), else the fallback figure."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"])
+    return FALLBACK_BF16_TFLOPS_SUSTAINED
+
+
+def prefill_flops(cfg, rows: int, prompt: int) -> float:
+    """Algorithmic FLOPs of a prefill of `rows` prompts of `prompt` tokens:
+    the four projections of every layer, causal attention (QK^T and PV over
+    the visible keys) and the lm_head of the last position."""
+    H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    nq, nkv, L = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.num_hidden_layers
+    M = rows * prompt
+    linear = 2.0 * M * H * (nq + 2 * nkv) * D + 2.0 * M * nq * D * H + 2.0 * M * H * 2 * I + 2.0 * M * I * H
+    attn = 4.0 * rows * nq * D * (prompt * (prompt + 1) / 2)
+    return L * (linear + attn) + 2.0 * rows * H * cfg.vocab_size
 
 
 # ---------------------------------------------------------------------------
@@ -440,6 +464,10 @@ def run_single(args) -> None:
         "prefill": {
             "tok_s": rows * args.prompt / (prefill_ms / 1000.0),
             "ms": prefill_ms,
+            "tflops": prefill_flops(cfg, rows, args.prompt) / (prefill_ms / 1000.0) / 1e12,
+            "sustained_peak_tflops": sustained_bf16_tflops(),
+            "frac_of_sustained": prefill_flops(cfg, rows, args.prompt) / (prefill_ms / 1000.0) / 1e12
+            / sustained_bf16_tflops(),
         },
         "gpu_launches": int(launches),
         "profile": prof,
