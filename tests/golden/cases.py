@@ -40,8 +40,8 @@ class Case:
         return torch.randint(0, self.cfg["vocab_size"], (self.batch, self.prompt), generator=g)
 
 
-# the tiny Llama, fp32, 2 stages, B=1, 64-token prompt,
-# 32 greedy decode steps.
+# The reference's own CPU-runnable case: the tiny Llama, fp32, 2 stages, B=1,
+# 64-token prompt, 32 greedy decode steps.
 C1 = Case(
     name="llama_c1_fp32",
     arch="llama",

@@ -75,7 +75,7 @@ def test_stage_path_matches_reference_and_oracle(case):
 
 
 def test_c1_free_running_greedy_is_token_identical():
-    """32 greedy steps, no teacher forcing."""
+    """The tiny fp32 Llama case: 32 greedy steps, no teacher forcing."""
     g = load_golden(C1.name)
     workers, _ = build(C1)
     with torch.no_grad():
