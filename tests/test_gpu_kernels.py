@@ -91,6 +91,18 @@ def test_linear_bf16_matches_fp32_reference(M, N, K, epilogue):
     check(y, ref, torch.bfloat16, {"store": 1, "resid": 2, "swiglu": 3}[epilogue])
 
 
+@pytest.mark.parametrize(
+    "M,N,K,epilogue",
+    [(8192, 6144, 4096, "store"), (8192, 4096, 14336, "resid"), (8192, 14336, 4096, "swiglu")],
+    ids=["qkv", "down", "gate_up"],
+)
+def test_linear_full_prefill_shapes_match_fp32_reference(M, N, K, epilogue):
+    """The Llama-3-8B prefill GEMMs at the benchmark's 8192 token rows: the
+    only sizes at which the CTA-pair kernel walks its tiles in more than one
+    L2 band."""
+    test_linear_bf16_matches_fp32_reference(M, N, K, epilogue)
+
+
 @pytest.mark.parametrize("M,N,K", [(33, 4096, 4096), (300, 688, 256), (1500, 2000, 512), (2048, 4096, 4096)])
 @pytest.mark.parametrize("epilogue", ["store", "resid", "swiglu"])
 def test_linear_single_sm_kernel_matches_fp32_reference(M, N, K, epilogue, monkeypatch):
