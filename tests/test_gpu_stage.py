@@ -309,18 +309,19 @@ def test_attention_over_imported_cache_matches_oracle(D, nq, nkv, T):
 # ---------------------------------------------------------------------------
 
 @pytest.mark.parametrize(
-    "dtype,D,nq,nkv,qk_norm",
+    "dtype,D,nq,nkv,qk_norm,S",
     [
-        (torch.float32, 128, 4, 2, True),    # a CTA per token, 32 lanes per head
-        (torch.float32, 64, 8, 2, False),    # 16 lanes per head
-        (torch.bfloat16, 128, 12, 4, True),  # 16 lanes per head, two rounds of the row
-        (torch.bfloat16, 64, 5, 1, False),   # 8 lanes per head, 7 heads: partial warps and groups
-        (torch.bfloat16, 32, 4, 2, False),   # head_dim outside the vector kernels
+        (torch.float32, 128, 4, 2, True, 40),    # a CTA per token, 32 lanes per head
+        (torch.float32, 64, 8, 2, False, 40),    # 16 lanes per head
+        (torch.bfloat16, 128, 12, 4, True, 40),  # 16 lanes per head, two rounds of the row
+        (torch.bfloat16, 64, 5, 1, False, 40),   # 8 lanes per head, 7 heads: partial warps and groups
+        (torch.bfloat16, 32, 4, 2, False, 40),   # head_dim outside the vector kernels
+        (torch.bfloat16, 128, 8, 2, False, 300), # more tokens than resident CTAs: each CTA takes several
     ],
-    ids=["f32-d128-qkn", "f32-d64", "bf16-d128-qkn", "bf16-d64-odd", "bf16-d32"],
+    ids=["f32-d128-qkn", "f32-d64", "bf16-d128-qkn", "bf16-d64-odd", "bf16-d32", "bf16-d128-600tok"],
 )
-def test_rope_kv_append_matches_oracle(dtype, D, nq, nkv, qk_norm):
-    """Prefill of 2 x 40 tokens (the many-token kernel) then two decode
+def test_rope_kv_append_matches_oracle(dtype, D, nq, nkv, qk_norm, S):
+    """Prefill of 2 x S tokens (the many-token kernel) then two decode
     steps (the decode-row kernel, reading the projection's pieces in bf16):
     the exported K / V cache and the logits against the oracle.  Cache bar:
     max |cuda - oracle| <= 1e-4 (fp32) or 2e-2 (bf16) x max |oracle|."""
@@ -333,8 +334,8 @@ def test_rope_kv_append_matches_oracle(dtype, D, nq, nkv, qk_norm):
     oracle = R.OracleStage(cfg, 0, 2, True, True, full, dtype)
     rel = 1e-4 if dtype == torch.float32 else 2e-2
     g = torch.Generator().manual_seed(D + nq)
-    stage.kv_reserve(1, 2, 64)
-    ids = torch.randint(0, cfg.vocab_size, (2, 40), generator=g)
+    stage.kv_reserve(1, 2, S + 8)
+    ids = torch.randint(0, cfg.vocab_size, (2, S), generator=g)
     steps = [ids] + [torch.randint(0, cfg.vocab_size, (2, 1), generator=g) for _ in range(2)]
     for i, x in enumerate(steps):
         got = stage.forward_slot(1, None, input_ids=x).float().cpu()
