@@ -647,13 +647,18 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
         MG_TIMED(MG_PROF_OTHER, norm_bytes, 0, launch_rmsnorm(dt, st->x, H, w.ln1, M, H, c.rms_norm_eps, st->xn, s), "input_layernorm");
       la.X = st->xn; la.ldx = H; la.W = w.wqkv; la.Y = st->qkv; la.ldy = st->Nqkv;
       la.N = st->Nqkv; la.K = H; la.epilogue = use_pieces ? kEpiPieces : kEpiStore; la.R = nullptr;
-      MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "qkv projection");
       qa.layer = l;
       qa.q_norm = w.qn;
       qa.k_norm = w.kn;
       qa.use_pieces = use_pieces;
       qa.pieces = pq;
-      MG_TIMED(MG_PROF_OTHER, 2.0 * M * st->Nqkv * st->esz, 0, launch_qkv_post(qa, s), "rope / kv append");
+      if (qkv_rope_fusable(la, qa)) {  // prefill: RoPE and the KV append in the projection's epilogue
+        MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_qkv_rope_kv(la, qa, s),
+                 "qkv projection + rope / kv append");
+      } else {
+        MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "qkv projection");
+        MG_TIMED(MG_PROF_OTHER, 2.0 * M * st->Nqkv * st->esz, 0, launch_qkv_post(qa, s), "rope / kv append");
+      }
       aa.layer = l;
       MG_TIMED(MG_PROF_ATTENTION, attn_bytes, attn_flops, launch_attention(aa, s), "attention");
       la.X = st->attn; la.ldx = qd; la.W = w.wo; la.Y = st->x; la.ldy = H;

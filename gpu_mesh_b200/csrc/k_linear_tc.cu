@@ -56,6 +56,9 @@ constexpr int kStages = 4;
 #define MG_GEMM_BAND_MB 32  // bytes of the reused operand per band of tiles (0: one band)
 #endif
 constexpr int kEpiWarps = MG_GEMM_EPI_WARPS;
+// The qkv projection with RoPE, QK-norm and the KV append in its epilogue
+// (prefill, head_dim 128; CTA-pair kernel only).  Local to this file.
+constexpr int kEpiRopeKv = 5;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
@@ -288,6 +291,125 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Epilogue of the qkv projection for one token row and one head of 128
+// columns (this warp's half of a 256-column tile): the accumulator rounded to
+// bf16 as the store epilogue would, then, as the RoPE / KV-append kernel does,
+// QK-norm (q / k heads, if the model has it), rotary embedding with the
+// rotate-half partner 64 columns away, and the store to the query buffer or
+// the slot's KV cache.  `trow` addresses this lane's TMEM row at the head's
+// first column; every lane runs the warp-collective TMEM loads.
+__device__ __forceinline__ void rope_kv_epilogue(const LinearArgs& a, const QkvPostArgs& qp, int row, int n,
+                                                 uint32_t trow) {
+  const int nh = qp.nq + 2 * qp.nkv;
+  const int hh = n / 128;
+  if (n >= a.N || hh >= nh) return;  // uniform over the warp
+  const bool live = row < a.M;
+  int cache_pos = 0;
+  int64_t pos = 0;
+  RowDesc rd{};
+  if (live) {
+    const int b = row / qp.S, s = row % qp.S;
+    rd = qp.rows[b];
+    cache_pos = rd.past + s;
+    pos = qp.positions ? qp.positions[row] : (int64_t)cache_pos;
+    if (pos < 0 || pos >= qp.max_pos) {
+      flag_error(qp.err, kErrPositionRange);
+      pos = pos < 0 ? 0 : qp.max_pos - 1;
+    }
+  }
+  const bool is_q = hh < qp.nq;
+  const bool is_k = !is_q && hh < qp.nq + qp.nkv;
+  bf16* kv = (bf16*)rd.kv_base;
+  bf16* dst = nullptr;
+  if (live) {
+    if (is_q)
+      dst = (bf16*)qp.q_out + ((size_t)row * qp.nq + hh) * 128;
+    else if (is_k)
+      dst = kv + kv_offset_elems(qp.layer, 0, rd.slot_rows, rd.row, qp.nkv, hh - qp.nq, rd.cap, 128, cache_pos);
+    else
+      dst = kv + kv_offset_elems(qp.layer, 1, rd.slot_rows, rd.row, qp.nkv, hh - qp.nq - qp.nkv, rd.cap, 128,
+                                 cache_pos);
+  }
+  float v[32], u[32];
+  if (!is_q && !is_k) {  // value head: the rounded accumulator, appended as is
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      __syncwarp();
+      tmem_ld32(trow + c, v);
+      if (!live) continue;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 o;
+        o.x = pack_bf16(v[i + 0], v[i + 1]);
+        o.y = pack_bf16(v[i + 2], v[i + 3]);
+        o.z = pack_bf16(v[i + 4], v[i + 5]);
+        o.w = pack_bf16(v[i + 6], v[i + 7]);
+        *reinterpret_cast<uint4*>(dst + c + i) = o;
+      }
+    }
+    return;
+  }
+  const bf16* nw = (const bf16*)(is_q ? qp.q_norm : qp.k_norm);
+  float r = 1.f;
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      __syncwarp();
+      tmem_ld32(trow + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float x = rt<bf16>(v[i]);
+        ss += x * x;
+      }
+    }
+    r = 1.0f / sqrtf(ss / 128.0f + qp.eps);
+  }
+  const bf16* cs = (const bf16*)qp.cos + (size_t)pos * 64;
+  const bf16* sn = (const bf16*)qp.sin + (size_t)pos * 64;
+#pragma unroll 1
+  for (int c = 0; c < 64; c += 32) {
+    __syncwarp();
+    tmem_ld32(trow + c, v);       // dims c .. c + 31
+    tmem_ld32(trow + c + 64, u);  // their rotate-half partners
+    if (!live) continue;
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      float cv[8], sv[8], gl[8], gh[8];
+      load16_f<bf16>(cs + c + i, cv);
+      load16_f<bf16>(sn + c + i, sv);
+      if (nw) {
+        load16_f<bf16>(nw + c + i, gl);
+        load16_f<bf16>(nw + c + 64 + i, gh);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float xl = rt<bf16>(v[i + e]), xh = rt<bf16>(u[i + e]);
+        if (nw) {
+          xl = rt<bf16>(rt<bf16>(xl * r) * gl[e]);
+          xh = rt<bf16>(rt<bf16>(xh * r) * gh[e]);
+        }
+        v[i + e] = rt<bf16>(xl * cv[e]) + rt<bf16>(-xh * sv[e]);
+        u[i + e] = rt<bf16>(xh * cv[e]) + rt<bf16>(xl * sv[e]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      uint4 o, p;
+      o.x = pack_bf16(v[i + 0], v[i + 1]);
+      o.y = pack_bf16(v[i + 2], v[i + 3]);
+      o.z = pack_bf16(v[i + 4], v[i + 5]);
+      o.w = pack_bf16(v[i + 6], v[i + 7]);
+      p.x = pack_bf16(u[i + 0], u[i + 1]);
+      p.y = pack_bf16(u[i + 2], u[i + 3]);
+      p.z = pack_bf16(u[i + 4], u[i + 5]);
+      p.w = pack_bf16(u[i + 6], u[i + 7]);
+      *reinterpret_cast<uint4*>(dst + c + i) = o;
+      *reinterpret_cast<uint4*>(dst + c + 64 + i) = p;
+    }
+  }
+}
+
 // CTA pairs (clusters of two SMs) on the 2-SM MMA: a tile is 256 rows of X
 // x 256 rows of W (SwiGLU: 128 gate + 128 up rows -> 128 outputs).  CTA r of
 // the pair loads X rows 128r .. 128r + 127 of the tile and W rows
@@ -323,7 +445,7 @@ struct PairSmem {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                     LinearArgs a, TileGrid tg, int* err) {
+                     LinearArgs a, TileGrid tg, int* err, const __grid_constant__ QkvPostArgs qp) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   using L = PairSmem;
@@ -469,6 +591,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = tg.m(t) * 256 + 128 * (int)rank + q * 32 + lane;
       const int n0 = tg.n(t) * NOUT;
       const uint32_t trow = tmem + lanes + b * BN;
+      if constexpr (EPI == kEpiRopeKv) {
+        rope_kv_epilogue(a, qp, row, n0 + half * 128, trow + half * 128);
+      } else {
 #pragma unroll 1
       for (int c = half * (NOUT / kParts); c < (half + 1) * (NOUT / kParts); c += 32) {
         float v[32], u[32];
@@ -502,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           o.w = pack_bf16(v[i + 6], v[i + 7]);
           *reinterpret_cast<uint4*>(y + i) = o;
         }
+      }
       }
       // This CTA's rows of the accumulator are stored: hand it back to the MMA warp.
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -568,7 +694,7 @@ cudaError_t launch_tc(const LinearArgs& a, cudaStream_t s) {
 }
 
 template <int EPI>
-cudaError_t launch_pair(const LinearArgs& a, cudaStream_t s) {
+cudaError_t launch_pair(const LinearArgs& a, cudaStream_t s, const QkvPostArgs* qp = nullptr) {
   CUtensorMap tx, tw;
   const uint64_t wrows = (EPI == kEpiSwiGLU) ? 2ull * a.N : (uint64_t)a.N;
   if (!make_map(&tx, a.X, a.M, a.K, a.ldx) || !make_map(&tw, a.W, wrows, a.K, a.K)) return cudaErrorInvalidValue;
@@ -620,7 +746,8 @@ cudaError_t launch_pair(const LinearArgs& a, cudaStream_t s) {
   const int pairs = (int)std::min<long long>(tiles, max_pairs[dev]);
   cfg.gridDim = dim3(2 * pairs);
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, tx, tw, a, tg, a.err);
+  const QkvPostArgs none{};
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, tx, tw, a, tg, a.err, qp ? *qp : none);
   note_launch();
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
@@ -653,6 +780,26 @@ cudaError_t launch_linear_tc(const LinearArgs& a, cudaStream_t s) {
     case kEpiResid: return launch_tc<256, kEpiResid>(a, s);
     default: return launch_tc<256, kEpiSwiGLU>(a, s);
   }
+}
+
+bool qkv_rope_fusable(const LinearArgs& a, const QkvPostArgs& q) {
+  return a.dtype == kBF16 && q.dtype == kBF16 && q.D == 128 && !q.use_pieces && a.epilogue == kEpiStore &&
+         a.Y == q.qkv && a.N == (q.nq + 2 * q.nkv) * 128 && a.M == q.B * q.S &&
+         linear_tc_applicable(a.dtype, a.M, a.N, a.K);
+}
+
+cudaError_t launch_qkv_rope_kv(const LinearArgs& a, const QkvPostArgs& q, cudaStream_t s) {
+  if (!qkv_rope_fusable(a, q)) return cudaErrorInvalidValue;
+  if (((uintptr_t)a.X % 16) || ((uintptr_t)a.W % 16) || (a.ldx % 8)) return cudaErrorInvalidValue;
+  const char* single = getenv("MESHGPU_GEMM_SINGLE_SM");
+  if (!(single && single[0] == '1')) {
+    const cudaError_t e = launch_pair<kEpiRopeKv>(a, s, &q);
+    if (e != cudaErrorNotSupported) return e;
+  }
+  // No CTA pair: the projection into the qkv buffer, then the RoPE / append kernel.
+  const cudaError_t e = launch_linear_tc(a, s);
+  if (e != cudaSuccess) return e;
+  return launch_qkv_post(q, s);
 }
 
 }  // namespace mg
