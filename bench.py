@@ -133,13 +133,18 @@ def prefill_flops(cfg, rows: int, prompt: int) -> float:
 # CPU baseline: the oracle (the reference's algorithm) on the host cores
 # ---------------------------------------------------------------------------
 
-def cpu_baseline(cfg, *, micro: int, context: int, steps: int, weights_from=None) -> dict:
-    """Time the CPU oracle on a bounded sample of the decode workload.
+def cpu_baseline(cfg, *, micro: int, micro_batches: int, context: int, steps: int, warmup: int = 1,
+                 weights_from=None) -> dict:
+    """Time the CPU oracle on the decode workload's own step.
 
-    Sample: one micro-batch of ``micro`` rows, every layer's KV cache pre-filled
-    to ``context`` positions with N(0, 1) bf16 values (the cost of a decode step
-    does not depend on how the prefix was produced), ``steps`` greedy decode
-    steps through all layers and the lm_head.
+    One step decodes one token for every row: ``micro_batches`` request
+    contexts of ``micro`` rows, each a separate KV cache, decoded one context
+    after the other through all layers and the lm_head, as the reference's
+    pipeline_decode_step does per cache_key.  Every layer's cache is
+    pre-filled to ``context`` positions with N(0, 1) bf16 values (the cost of
+    a decode step does not depend on how the prefix was produced, and a CPU
+    prefill of the prompts would take hours).  ``warmup`` untimed steps, then
+    exactly ``steps`` timed steps.
     """
     from oracle import stage_ref as R
 
@@ -156,29 +161,40 @@ def cpu_baseline(cfg, *, micro: int, context: int, steps: int, weights_from=None
             state[local] = synthetic_tensor(global_key, shape, seed=0, dtype=torch.bfloat16, device=dev).cpu()
     st = R.OracleStage(cfg, 0, cfg.num_hidden_layers, True, True, state, torch.bfloat16)
     g = torch.Generator().manual_seed(0)
-    kv = []
-    for _ in range(cfg.num_hidden_layers):
-        shape = (micro, cfg.num_key_value_heads, context, cfg.head_dim)
-        kv.append((torch.randn(shape, generator=g).to(torch.bfloat16),
-                   torch.randn(shape, generator=g).to(torch.bfloat16)))
-    st.caches["b"] = kv
-    ids = torch.randint(0, cfg.vocab_size, (micro, 1), generator=g)
+    keys = [f"mb{i}" for i in range(micro_batches)]
+    ids = {}
+    for key in keys:
+        kv = []
+        for _ in range(cfg.num_hidden_layers):
+            shape = (micro, cfg.num_key_value_heads, context, cfg.head_dim)
+            kv.append((torch.randn(shape, generator=g).to(torch.bfloat16),
+                       torch.randn(shape, generator=g).to(torch.bfloat16)))
+        st.caches[key] = kv
+        ids[key] = torch.randint(0, cfg.vocab_size, (micro, 1), generator=g)
+
+    def step() -> None:
+        for key in keys:
+            logits = st.forward(input_ids=ids[key], key=key)
+            ids[key] = R.greedy(logits[:, -1]).unsqueeze(-1)
+
     with torch.no_grad():
-        st.forward(input_ids=ids, key="b")  # warm-up
-        st.trim(context, "b")
+        for _ in range(warmup):
+            step()
         t0 = time.perf_counter()
         for _ in range(steps):
-            logits = st.forward(input_ids=ids, key="b")
-            ids = R.greedy(logits[:, -1]).unsqueeze(-1)
+            step()
         dt = time.perf_counter() - t0
+    rows = micro * micro_batches
     return {
-        "value": micro * steps / dt,
+        "value": rows * steps / dt,
         "unit": "tok/s",
         "cores": threads,
         "kind": "port",
-        "sample": (f"oracle (CPU restatement of the reference stage), Llama-3-8B bf16, {micro} rows, "
-                   f"KV pre-filled to {context} positions, {steps} greedy decode steps, "
-                   f"{threads} threads"),
+        "sample": (f"oracle (CPU restatement of the reference stage), {cfg.num_hidden_layers} layers bf16, "
+                   f"{rows} rows as {micro_batches} request contexts of {micro} decoded one after the other, "
+                   f"KV pre-filled to {context} positions with N(0,1), {warmup} untimed + {steps} timed "
+                   f"greedy decode steps, {threads} threads"),
+        "steps": steps,
         "seconds": dt,
     }
 
@@ -188,17 +204,21 @@ def run_reference_arm(args) -> None:
     if rank != 0:
         return
     cfg = model_config(args.model, args.layers)
-    base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=max(1, min(args.steps, 2)))
-    steps = args.steps
+    # The reference's algorithm on the host cores: exactly --steps timed steps of
+    # the full batch (all rows, every context), after one untimed step.
+    base = cpu_baseline(cfg, micro=args.micro, micro_batches=args.micro_batches, context=args.prompt,
+                        steps=args.steps, warmup=1)
+    rows = args.micro * args.micro_batches
     line = {
         "impl": "reference",
         "metric": metric_for(args),
         "value": base["value"],
         "unit": "tok/s",
         "n_gpus": args.gpus,
-        "steps": steps,
-        "warmup": args.warmup,
-        "ms_per_step": 1000.0 * args.micro / base["value"],
+        "steps": base["steps"],
+        "warmup": 1,
+        "ms_per_step": 1000.0 * base["seconds"] / base["steps"],
+        "rows_per_step": rows,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -407,7 +427,9 @@ def run_single(args) -> None:
 
     base = None
     if not args.no_cpu_baseline:
-        base = cpu_baseline(cfg, micro=args.micro, context=args.prompt, steps=2)
+        # bounded sample: 3 steps of the full batch (about 10 s of CPU work)
+        base = cpu_baseline(cfg, micro=args.micro, micro_batches=args.micro_batches, context=args.prompt,
+                            steps=3, warmup=1)
 
     traffic = NCU_TRAFFIC if args.model == "llama3-8b" else {
         k: {"dram_bytes": None, "algorithmic_bytes": None, "launches": None} for k in NCU_TRAFFIC}

@@ -26,6 +26,9 @@ MG_OUT_HIDDEN = 0
 MG_OUT_LOGITS_ALL = 1
 MG_OUT_LOGITS_LAST = 2
 
+(MG_W_EMBED, MG_W_NORM, MG_W_LM_HEAD, MG_W_INPUT_NORM, MG_W_QKV, MG_W_Q_NORM, MG_W_K_NORM, MG_W_O,
+ MG_W_POST_NORM, MG_W_GATE_UP, MG_W_DOWN) = range(11)
+
 MG_ATTN_SDPA = 0
 MG_ATTN_EAGER = 1
 MG_ATTN_CACHE_CAUSAL = 2
@@ -190,6 +193,10 @@ SIGNATURES["mg_linear"] = (
     [_i32, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, ctypes.c_uint64, _vp],
 )
 SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i32])
+SIGNATURES["mg_linear_check_device"] = (ctypes.c_int, [_vp])
+SIGNATURES["mg_stage_weight"] = (ctypes.c_int, [_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)])
+SIGNATURES["mg_peer_access"] = (ctypes.c_int, [_i32, _i32, ctypes.POINTER(ctypes.c_int32)])
+SIGNATURES["mg_peer_copy"] = (ctypes.c_int, [_vp, _i32, _vp, _i32, ctypes.c_uint64, _vp])
 SIGNATURES["mg_linear_noalloc"] = (
     ctypes.c_int,
     [_i32, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp],

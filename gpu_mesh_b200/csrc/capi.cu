@@ -1093,6 +1093,29 @@ int mg_stage_decode_greedy(mg_stage* st, const int32_t* slots, int32_t n_slots, 
   return decode_slots(st, slots, n_slots, ids, hidden_in, MG_OUT_LOGITS_ALL, logits_out, ids_out, stream);
 }
 
+int mg_stage_weight(const mg_stage* st, int32_t which, int32_t layer, void** ptr) {
+  if (!st || !ptr) return fail(MG_EINVAL, "null argument");
+  *ptr = nullptr;
+  const bool per_layer = which >= MG_W_INPUT_NORM && which <= MG_W_DOWN;
+  if (per_layer && (layer < 0 || layer >= (int)st->layers.size()))
+    return fail(MG_EINVAL, "local layer %d outside [0, %d)", layer, (int)st->layers.size());
+  switch (which) {
+    case MG_W_EMBED: *ptr = st->embed; break;
+    case MG_W_NORM: *ptr = st->norm; break;
+    case MG_W_LM_HEAD: *ptr = st->lm_head; break;
+    case MG_W_INPUT_NORM: *ptr = st->layers[layer].ln1; break;
+    case MG_W_QKV: *ptr = st->layers[layer].wqkv; break;
+    case MG_W_Q_NORM: *ptr = st->layers[layer].qn; break;
+    case MG_W_K_NORM: *ptr = st->layers[layer].kn; break;
+    case MG_W_O: *ptr = st->layers[layer].wo; break;
+    case MG_W_POST_NORM: *ptr = st->layers[layer].ln2; break;
+    case MG_W_GATE_UP: *ptr = st->layers[layer].wgu; break;
+    case MG_W_DOWN: *ptr = st->layers[layer].wd; break;
+    default: return fail(MG_EINVAL, "unknown weight %d", which);
+  }
+  return MG_OK;
+}
+
 int mg_stage_check_device(mg_stage* st, void* stream) {
   if (!st) return fail(MG_EINVAL, "null stage");
   DeviceGuard guard(st->cfg.device);
@@ -1143,6 +1166,53 @@ uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32
   return linear_scratch_elems(dtype, M, N, K, epilogue);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Error word of the standalone linear entry points (mg_linear and
+// mg_linear_noalloc): a bounded wait inside the decode GEMM that runs out
+// records code 3 here instead of in a stage's word.  A file-scope device
+// array, so it needs no allocation; its address is looked up per device.
+// ---------------------------------------------------------------------------
+namespace {
+
+static __device__ int g_linear_err;
+
+struct SymbolCache {
+  void* ptr[64] = {};
+  std::mutex mu;
+};
+
+// Device address of `symbol` on the current device.  In host code a
+// __device__ variable's name is a host-side stand-in, never device memory, so
+// the address must come from cudaGetSymbolAddress.  Looked up again on every
+// call outside stream capture (cheap once the module is loaded, and it follows
+// a cudaDeviceReset); during capture the last looked-up address is used.
+int symbol_address(SymbolCache& cache, const void* symbol, cudaStream_t stream, void** out,
+                   const char* what) {
+  int dev = -1;
+  MG_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(MG_EINVAL, "device ordinal %d out of range", dev);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  MG_CUDA(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");
+  std::lock_guard<std::mutex> lock(cache.mu);
+  if (cap == cudaStreamCaptureStatusNone) {
+    void* p = nullptr;
+    MG_CUDA(cudaGetSymbolAddress(&p, symbol), what);
+    cache.ptr[dev] = p;
+  } else if (!cache.ptr[dev]) {
+    return fail(MG_ESTATE, "%s: make one call on this device before capturing a stream", what);
+  }
+  *out = cache.ptr[dev];
+  return MG_OK;
+}
+
+SymbolCache g_linear_err_addr;
+
+}  // namespace
+
+extern "C" {
+
 int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t M, int32_t N,
               int32_t K, int32_t epilogue, const void* R, int64_t ldr, void* Y, int64_t ldy,
               float* scratch, uint64_t scratch_elems, void* stream) {
@@ -1163,8 +1233,56 @@ int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t 
   la.M = M; la.N = N; la.K = K; la.epilogue = epilogue;
   la.partial = scratch;
   la.partial_elems = scratch_elems;
-  la.err = nullptr;
+  void* err = nullptr;
+  int rc = symbol_address(g_linear_err_addr, (const void*)&g_linear_err, (cudaStream_t)stream, &err,
+                          "cudaGetSymbolAddress(linear error word)");
+  if (rc) return rc;
+  la.err = (int*)err;
   MG_LAUNCH(launch_linear(la, (cudaStream_t)stream), "linear");
+  return MG_OK;
+}
+
+int mg_linear_check_device(void* stream) {
+  void* err = nullptr;
+  int rc = symbol_address(g_linear_err_addr, (const void*)&g_linear_err, (cudaStream_t)stream, &err,
+                          "cudaGetSymbolAddress(linear error word)");
+  if (rc) return rc;
+  int h = 0;
+  MG_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+          "linear error word read");
+  MG_CUDA(cudaStreamSynchronize((cudaStream_t)stream), "linear error word sync");
+  if (h == kErrNone) return MG_OK;
+  MG_CUDA(cudaMemset(err, 0, sizeof(int)), "linear error word reset");
+  return fail(MG_EDEVICE, "a linear launch gave up waiting for its data (code %d); its output is invalid", h);
+}
+
+int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled) {
+  if (!enabled) return fail(MG_EINVAL, "null argument");
+  *enabled = 0;
+  if (device == peer) {
+    *enabled = 1;
+    return MG_OK;
+  }
+  int can = 0;
+  MG_CUDA(cudaDeviceCanAccessPeer(&can, device, peer), "cudaDeviceCanAccessPeer");
+  if (!can) return MG_OK;  // copies between the pair stage through the host
+  DeviceGuard guard(device);
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();  // clear the (non-sticky) "already enabled" error
+  } else if (e != cudaSuccess) {
+    return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+  }
+  *enabled = 1;
+  return MG_OK;
+}
+
+int mg_peer_copy(void* dst, int32_t dst_device, const void* src, int32_t src_device, uint64_t bytes,
+                 void* stream) {
+  if ((!dst || !src) && bytes) return fail(MG_EINVAL, "null buffer");
+  if (bytes == 0) return MG_OK;
+  MG_CUDA(cudaMemcpyPeerAsync(dst, dst_device, src, src_device, (size_t)bytes, (cudaStream_t)stream),
+          "cudaMemcpyPeerAsync");
   return MG_OK;
 }
 
@@ -1201,25 +1319,9 @@ namespace {
 constexpr size_t kNoAllocScratch = MG_LINEAR_NOALLOC_SCRATCH;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratch];
 
-// Device address of this process's copy of the array, per device.  In host
-// code `g_noalloc_scratch` names a host-side stand-in, never the device
-// memory, so the address must come from cudaGetSymbolAddress.
-float* g_noalloc_ptr[64] = {};
-std::mutex g_noalloc_mu;
-
-int noalloc_scratch(float** out) {
-  int dev = -1;
-  MG_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(MG_EINVAL, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    MG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
-    g_noalloc_ptr[dev] = (float*)p;
-  }
-  *out = g_noalloc_ptr[dev];
-  return MG_OK;
-}
+// Device address of this process's copy of the array on the current device
+// (symbol_address: looked up again outside stream capture).
+SymbolCache g_noalloc_addr;
 
 }  // namespace
 
@@ -1233,9 +1335,10 @@ extern "C" int mg_linear_noalloc(int32_t dtype, const void* X, int64_t ldx, cons
                 "this shape needs %llu fp32 elements of split-K scratch; mg_linear_noalloc holds "
                 "%llu (use mg_linear with caller scratch)",
                 (unsigned long long)need, (unsigned long long)kNoAllocScratch);
-  float* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
+  void* scratch = nullptr;
+  int rc = symbol_address(g_noalloc_addr, (const void*)g_noalloc_scratch, (cudaStream_t)stream, &scratch,
+                          "cudaGetSymbolAddress(noalloc scratch)");
   if (rc) return rc;
-  return mg_linear(dtype, X, ldx, W, M, N, K, epilogue, R, ldr, Y, ldy, scratch, kNoAllocScratch,
-                   stream);
+  return mg_linear(dtype, X, ldx, W, M, N, K, epilogue, R, ldr, Y, ldy, (float*)scratch,
+                   kNoAllocScratch, stream);
 }

@@ -1,24 +1,36 @@
 """Pipeline coordinator over B200 stages.
 
-Same contract as the reference's portable coordinator
-(src/meshgpu/backends/portable/pipeline.py):
-  * ``build_pipeline`` splits layers evenly, remainder to the first stages,
-    stage 0 with the embedding and the last stage with norm + lm_head (:48-103);
-  * ``pipeline_prefill`` clears the context on every stage, runs stages in
-    order and clears again on failure (:110-163);
-  * ``pipeline_decode_step`` checks that every stage holds the same cached
-    length, feeds positions arange(T, T+S) and trims back on failure (:166-233);
-  * async variants run local stage calls in a worker thread and drain them on
-    cancellation (:240-377).
-The coordinator functions are duck-typed: they drive reference workers and
-B200 workers alike.
+The contract is the reference's portable coordinator
+(src/meshgpu/backends/portable/pipeline.py): ``build_pipeline`` splits layers
+evenly with the remainder to the first stages (:48-103); ``pipeline_prefill``
+clears the context on every stage, runs the stages in order and clears again
+on failure (:110-163); ``pipeline_decode_step`` requires every stage to hold
+the same cached length, feeds positions arange(T, T+S) and trims back on
+failure (:166-233); the async variants drain a running stage call before a
+cancellation propagates (:240-377).  Arguments, results, messages and
+exception types are the reference's; the functions are duck-typed and drive
+reference workers and B200 workers alike.
+
+How a call runs is this module's own.  Each coordinator function is a *plan*:
+a generator that validates its arguments, yields the stage calls it needs
+(``_Call``) one at a time, receives their results, and on failure yields its
+rollback calls before re-raising.  One plan serves both drivers:
+``_run_plan`` calls the stages directly, and ``_run_plan_async`` either runs
+the whole synchronous driver in one worker thread (every stage local) or
+awaits the calls one by one (remote stages with coroutine methods).  Between
+B200 stages on different GPUs the boundary tensor moves through
+``gpu_mesh_b200.boundary`` (a side-stream peer copy ordered by events), and
+``gpu_mesh_b200.schedule.MicroBatchPipeline`` keeps several micro-batches in
+flight across the stages.
 """
 from __future__ import annotations
 
 import asyncio
 import inspect
 import logging
-from collections.abc import Sequence
+import threading
+from collections.abc import Generator, Sequence
+from dataclasses import dataclass, field
 from typing import Any
 
 import torch
@@ -120,7 +132,107 @@ def from_reference_workers(
 
 
 # ---------------------------------------------------------------------------
-# In-process pipeline inference
+# Plans and their drivers
+# ---------------------------------------------------------------------------
+
+@dataclass
+class _Call:
+    """One stage method call a plan needs; ``best_effort`` calls are rollback
+    steps whose failure is logged and answered with ``None``."""
+
+    worker: Any
+    method: str
+    args: tuple = ()
+    kwargs: dict = field(default_factory=dict)
+    best_effort: bool = False
+
+
+Plan = Generator[_Call, Any, Any]
+
+
+def _invoke(call: _Call) -> Any:
+    return getattr(call.worker, call.method)(*call.args, **call.kwargs)
+
+
+def _run_plan(plan: Plan, cancelled: threading.Event | None = None) -> Any:
+    """Drive a plan with direct (blocking) stage calls.  Once ``cancelled`` is
+    set, the plan gets a CancelledError at its next stage-call boundary, so it
+    rolls back the way an awaited plan does."""
+    try:
+        call = next(plan)
+        while True:
+            try:
+                result = _invoke(call)
+            except Exception as exc:
+                if not call.best_effort:
+                    call = plan.throw(exc)
+                    continue
+                log.warning("rollback step %s failed: %s", call.method, exc)
+                result = None
+            except BaseException as exc:  # KeyboardInterrupt and the like: roll back, then re-raise
+                call = plan.throw(exc)
+                continue
+            if cancelled is not None and cancelled.is_set() and not call.best_effort:
+                call = plan.throw(asyncio.CancelledError())
+                continue
+            call = plan.send(result)
+    except StopIteration as done:
+        return done.value
+
+
+def _has_coroutines(workers: Sequence[Any]) -> bool:
+    return any(
+        inspect.iscoroutinefunction(getattr(w, name, None))
+        for w in workers
+        for name in ("forward_inference", "clear_kv", "trim_kv", "kv_cache_length")
+    )
+
+
+async def _drained(fn, *args, cancelled: threading.Event | None = None) -> Any:
+    """Run a blocking function in a worker thread.  A cancellation sets
+    ``cancelled`` and waits for the function to finish before it propagates,
+    so nothing that follows races a stage call still running on the GPU."""
+    task = asyncio.ensure_future(asyncio.to_thread(fn, *args))
+    try:
+        return await asyncio.shield(task)
+    except asyncio.CancelledError:
+        if cancelled is not None:
+            cancelled.set()
+        await asyncio.wait([task])
+        raise
+
+
+async def _run_plan_async(plan: Plan, workers: Sequence[Any]) -> Any:
+    if not _has_coroutines(workers):
+        # Every stage is in this process: one thread hop for the whole call; a
+        # cancellation reaches the plan at its next stage-call boundary.
+        cancelled = threading.Event()
+        return await _drained(_run_plan, plan, cancelled, cancelled=cancelled)
+    try:
+        call = next(plan)
+        while True:
+            try:
+                fn = getattr(call.worker, call.method)
+                if inspect.iscoroutinefunction(fn):
+                    result = await fn(*call.args, **call.kwargs)
+                else:
+                    result = await _drained(_invoke, call)
+            except Exception as exc:
+                if not call.best_effort:
+                    call = plan.throw(exc)
+                    continue
+                log.warning("rollback step %s failed: %s", call.method, exc)
+                result = None
+            except BaseException as exc:  # cancellation: roll back, then propagate
+                call = plan.throw(exc)
+                continue
+            call = plan.send(result)
+    except StopIteration as done:
+        return done.value
+
+
+# ---------------------------------------------------------------------------
+# Argument checks (the reference's messages)
 # ---------------------------------------------------------------------------
 
 def _max_positions(worker: Any) -> int | None:
@@ -131,9 +243,134 @@ def _max_positions(worker: Any) -> int | None:
     return getattr(worker, "max_position_embeddings", None)
 
 
-def _extra(worker: Any, logits: str) -> dict[str, Any]:
+def _check_prompt(workers: Sequence[Any], input_ids: torch.Tensor) -> None:
+    if input_ids.ndim != 2:
+        raise ValueError("input_ids must have shape [batch, sequence]")
+    if input_ids.shape[0] < 1 or input_ids.shape[1] < 1:
+        raise ValueError("input_ids must have a non-empty batch and sequence")
+    if not workers:
+        raise ValueError("workers must not be empty")
+    limit = _max_positions(workers[0])
+    if limit is not None and input_ids.shape[1] > limit:
+        raise ValueError(f"prefill sequence length {input_ids.shape[1]} exceeds model context {limit}")
+
+
+def _check_next(workers: Sequence[Any], next_token: torch.Tensor) -> None:
+    if next_token.ndim != 2 or next_token.shape[0] < 1 or next_token.shape[1] < 1:
+        raise ValueError("next_token must have shape [batch, sequence] with sequence >= 1")
+    if not workers:
+        raise ValueError("workers must not be empty")
+
+
+def _checked_lengths(
+    lengths: list[int], query_len: int, max_positions: int | None, name: str, prefill_name: str
+) -> list[int]:
+    """Every stage must hold the same non-empty context with room for the query."""
+    for i, kv_len in enumerate(lengths):
+        if kv_len != lengths[0]:
+            raise RuntimeError(
+                "pipeline KV caches are out of sync: "
+                f"stage 0 has {lengths[0]} tokens, stage {i} has {kv_len}"
+            )
+        if kv_len == 0:
+            raise RuntimeError(f"{name} requires a prefilled KV cache; call {prefill_name} first")
+        if max_positions is not None and kv_len + query_len > max_positions:
+            raise ValueError(
+                f"decode would reach position {kv_len + query_len - 1}, "
+                f"beyond model context {max_positions}"
+            )
+    return lengths
+
+
+def _logits_kw(worker: Any, logits: str) -> dict[str, Any]:
     return {"logits": logits} if logits != "all" and isinstance(worker, B200StageWorker) else {}
 
+
+def _restore(workers: Sequence[Any], lengths: Sequence[int], cache_key: str | None) -> Plan:
+    """Rollback: every stage back to its length before the failed call."""
+    for worker, length in zip(workers, lengths):
+        if length == 0:
+            yield _Call(worker, "clear_kv", (cache_key,), best_effort=True)
+        else:
+            yield _Call(worker, "trim_kv", (length, cache_key), best_effort=True)
+
+
+# ---------------------------------------------------------------------------
+# The coordinator's plans
+# ---------------------------------------------------------------------------
+
+def _prefill_plan(workers, input_ids, operation_id, attempt_id, cache_key, logits="all") -> Plan:
+    _check_prompt(workers, input_ids)
+    for worker in workers:
+        yield _Call(worker, "clear_kv", (cache_key,))
+    hidden = None
+    try:
+        for i, worker in enumerate(workers):
+            kw = dict(input_ids=input_ids if i == 0 else None, operation_id=operation_id,
+                      attempt_id=attempt_id, reset_kv=False, cache_key=cache_key)
+            if i == len(workers) - 1:
+                kw.update(_logits_kw(worker, logits))
+            hidden = (yield _Call(worker, "forward_inference", (hidden,), kw)).output
+    except BaseException:
+        yield from _restore(workers, [0] * len(workers), cache_key)
+        raise
+    return hidden
+
+
+def _decode_plan(workers, next_token, operation_id, attempt_id, cache_key, logits="all",
+                 names=("pipeline_decode_step", "pipeline_prefill")) -> Plan:
+    _check_next(workers, next_token)
+    batch, query_len = next_token.shape
+    lengths = []
+    for worker in workers:
+        lengths.append(int((yield _Call(worker, "kv_cache_length", (cache_key,)))))
+    _checked_lengths(lengths, query_len, _max_positions(workers[0]), *names)
+    hidden = None
+    try:
+        for i, worker in enumerate(workers):
+            positions = torch.arange(lengths[i], lengths[i] + query_len, dtype=torch.long,
+                                     device=next_token.device).unsqueeze(0).expand(batch, -1)
+            kw = dict(input_ids=next_token if i == 0 else None, position_ids=positions,
+                      operation_id=operation_id, attempt_id=attempt_id, reset_kv=False,
+                      cache_key=cache_key)
+            if i == len(workers) - 1:
+                kw.update(_logits_kw(worker, logits))
+            hidden = (yield _Call(worker, "forward_inference", (hidden,), kw)).output
+    except BaseException:
+        yield from _restore(workers, lengths, cache_key)
+        raise
+    return hidden
+
+
+def _multi_plan(workers, next_tokens, cache_keys, name, last_call) -> Plan:
+    """One decode token for several contexts in one pass per stage; the last
+    stage runs ``last_call`` (``decode_multi`` or ``decode_greedy``)."""
+    if next_tokens.ndim != 2 or next_tokens.shape[1] != 1:
+        raise ValueError("next_tokens must have shape [rows, 1]")
+    if not workers:
+        raise ValueError("workers must not be empty")
+    limit = _max_positions(workers[0])
+    lengths = {}
+    for key in cache_keys:
+        lengths[key] = _checked_lengths([w.kv_cache_length(key) for w in workers], 1, limit, name,
+                                        "pipeline_prefill")
+    keys = list(cache_keys)
+    hidden = None
+    try:
+        for i, worker in enumerate(workers):
+            ids = next_tokens if i == 0 else None
+            if i == len(workers) - 1:
+                return (yield last_call(worker, hidden, keys, ids))
+            hidden = yield _Call(worker, "decode_multi", (hidden, keys), dict(input_ids=ids))
+    except BaseException:
+        for key, lens in lengths.items():
+            yield from _restore(workers, lens, key)
+        raise
+
+
+# ---------------------------------------------------------------------------
+# Public coordinator functions
+# ---------------------------------------------------------------------------
 
 @torch.no_grad()
 def pipeline_prefill(
@@ -147,36 +384,7 @@ def pipeline_prefill(
 ) -> torch.Tensor:
     """Prefill through all stages in order; logits [B, S, V] (or [B, 1, V]
     with ``logits="last"``)."""
-    if input_ids.ndim != 2:
-        raise ValueError("input_ids must have shape [batch, sequence]")
-    B, S = input_ids.shape
-    if B < 1 or S < 1:
-        raise ValueError("input_ids must have a non-empty batch and sequence")
-    if not workers:
-        raise ValueError("workers must not be empty")
-    max_positions = _max_positions(workers[0])
-    if max_positions is not None and S > max_positions:
-        raise ValueError(f"prefill sequence length {S} exceeds model context {max_positions}")
-    for w in workers:
-        w.clear_kv(cache_key)
-    hidden = None
-    try:
-        for i, worker in enumerate(workers):
-            result = worker.forward_inference(
-                hidden,
-                input_ids=input_ids if i == 0 else None,
-                operation_id=operation_id,
-                attempt_id=attempt_id,
-                reset_kv=False,
-                cache_key=cache_key,
-                **(_extra(worker, logits) if i == len(workers) - 1 else {}),
-            )
-            hidden = result.output
-    except BaseException:
-        _clear_kv_best_effort(workers, cache_key)
-        raise
-    assert hidden is not None
-    return hidden
+    return _run_plan(_prefill_plan(workers, input_ids, operation_id, attempt_id, cache_key, logits))
 
 
 @torch.no_grad()
@@ -190,39 +398,7 @@ def pipeline_decode_step(
     logits: str = "all",
 ) -> torch.Tensor:
     """One decode step over prefilled caches; logits [B, S, V]."""
-    if next_token.ndim != 2 or next_token.shape[0] < 1 or next_token.shape[1] < 1:
-        raise ValueError("next_token must have shape [batch, sequence] with sequence >= 1")
-    batch_size, query_len = next_token.shape
-    if not workers:
-        raise ValueError("workers must not be empty")
-    max_positions = _max_positions(workers[0])
-    cache_lengths = _checked_lengths(
-        [w.kv_cache_length(cache_key) for w in workers], query_len, max_positions, "pipeline_decode_step",
-        "pipeline_prefill",
-    )
-    hidden = None
-    try:
-        for i, worker in enumerate(workers):
-            kv_len = cache_lengths[i]
-            position_ids = torch.arange(
-                kv_len, kv_len + query_len, dtype=torch.long, device=next_token.device
-            ).unsqueeze(0).expand(batch_size, -1)
-            result = worker.forward_inference(
-                hidden,
-                input_ids=next_token if i == 0 else None,
-                position_ids=position_ids,
-                operation_id=operation_id,
-                attempt_id=attempt_id,
-                reset_kv=False,
-                cache_key=cache_key,
-                **(_extra(worker, logits) if i == len(workers) - 1 else {}),
-            )
-            hidden = result.output
-    except BaseException:
-        _restore_kv_lengths_best_effort(workers, cache_lengths, cache_key)
-        raise
-    assert hidden is not None
-    return hidden
+    return _run_plan(_decode_plan(workers, next_token, operation_id, attempt_id, cache_key, logits))
 
 
 @torch.no_grad()
@@ -241,30 +417,10 @@ def pipeline_decode_multi(
     ``pipeline_decode_step`` per context (the reference drives one context at
     a time, inference/batcher.py:229-247).  Rolls every context back on failure.
     """
-    if next_tokens.ndim != 2 or next_tokens.shape[1] != 1:
-        raise ValueError("next_tokens must have shape [rows, 1]")
-    if not workers:
-        raise ValueError("workers must not be empty")
-    max_positions = _max_positions(workers[0])
-    lengths = {}
-    for key in cache_keys:
-        lengths[key] = _checked_lengths(
-            [w.kv_cache_length(key) for w in workers], 1, max_positions,
-            "pipeline_decode_multi", "pipeline_prefill",
-        )
-    hidden = None
-    try:
-        for i, worker in enumerate(workers):
-            hidden = worker.decode_multi(
-                hidden, list(cache_keys), input_ids=next_tokens if i == 0 else None,
-                logits=logits,
-            )
-    except BaseException:
-        for key, lens in lengths.items():
-            _restore_kv_lengths_best_effort(workers, lens, key)
-        raise
-    assert hidden is not None
-    return hidden
+    def last(worker, hidden, keys, ids):
+        return _Call(worker, "decode_multi", (hidden, keys), dict(input_ids=ids, logits=logits))
+
+    return _run_plan(_multi_plan(workers, next_tokens, cache_keys, "pipeline_decode_multi", last))
 
 
 @torch.no_grad()
@@ -281,60 +437,11 @@ def pipeline_decode_greedy(
     ``greedy_sample`` of the logits (inference/sampling.py:45-56), which is
     what the reference's decode loops apply to the returned logits
     (session.py:245-259, batcher.py:356-388)."""
-    if next_tokens.ndim != 2 or next_tokens.shape[1] != 1:
-        raise ValueError("next_tokens must have shape [rows, 1]")
-    if not workers:
-        raise ValueError("workers must not be empty")
-    max_positions = _max_positions(workers[0])
-    lengths = {}
-    for key in cache_keys:
-        lengths[key] = _checked_lengths(
-            [w.kv_cache_length(key) for w in workers], 1, max_positions,
-            "pipeline_decode_greedy", "pipeline_prefill",
-        )
-    hidden = None
-    try:
-        for i, worker in enumerate(workers[:-1]):
-            hidden = worker.decode_multi(
-                hidden, list(cache_keys), input_ids=next_tokens if i == 0 else None,
-            )
-        return workers[-1].decode_greedy(
-            hidden, list(cache_keys), input_ids=next_tokens if len(workers) == 1 else None,
-            return_logits=return_logits,
-        )
-    except BaseException:
-        for key, lens in lengths.items():
-            _restore_kv_lengths_best_effort(workers, lens, key)
-        raise
+    def last(worker, hidden, keys, ids):
+        return _Call(worker, "decode_greedy", (hidden, keys), dict(input_ids=ids, return_logits=return_logits))
 
+    return _run_plan(_multi_plan(workers, next_tokens, cache_keys, "pipeline_decode_greedy", last))
 
-def _checked_lengths(
-    lengths: list[int], query_len: int, max_positions: int | None, name: str, prefill_name: str
-) -> list[int]:
-    expected = None
-    for i, kv_len in enumerate(lengths):
-        if expected is None:
-            expected = kv_len
-        elif kv_len != expected:
-            raise RuntimeError(
-                "pipeline KV caches are out of sync: "
-                f"stage 0 has {expected} tokens, stage {i} has {kv_len}"
-            )
-        if kv_len == 0:
-            raise RuntimeError(
-                f"{name} requires a prefilled KV cache; call {prefill_name} first"
-            )
-        if max_positions is not None and kv_len + query_len > max_positions:
-            raise ValueError(
-                f"decode would reach position {kv_len + query_len - 1}, "
-                f"beyond model context {max_positions}"
-            )
-    return lengths
-
-
-# ---------------------------------------------------------------------------
-# Async variants (local or remote stages)
-# ---------------------------------------------------------------------------
 
 async def pipeline_prefill_async(
     workers: list[Any],
@@ -344,33 +451,10 @@ async def pipeline_prefill_async(
     attempt_id: str = "a0",
     cache_key: str | None = None,
 ) -> torch.Tensor:
-    if input_ids.ndim != 2:
-        raise ValueError("input_ids must have shape [batch, sequence]")
-    if input_ids.shape[0] < 1 or input_ids.shape[1] < 1:
-        raise ValueError("input_ids must have a non-empty batch and sequence")
-    if not workers:
-        raise ValueError("workers must not be empty")
-    max_positions = _max_positions(workers[0])
-    if max_positions is not None and input_ids.shape[1] > max_positions:
-        raise ValueError(
-            f"prefill sequence length {input_ids.shape[1]} exceeds model context {max_positions}"
-        )
-    for worker in workers:
-        await _async_stage_call(worker, "clear_kv", cache_key)
-    hidden = None
-    try:
-        for index, worker in enumerate(workers):
-            result = await _async_stage_call(
-                worker, "forward_inference", hidden,
-                input_ids=input_ids if index == 0 else None,
-                operation_id=operation_id, attempt_id=attempt_id, reset_kv=False, cache_key=cache_key,
-            )
-            hidden = result.output
-    except BaseException:
-        await _clear_kv_async_best_effort(workers, cache_key)
-        raise
-    assert hidden is not None
-    return hidden
+    """``pipeline_prefill`` for local or remote (coroutine) stages."""
+    with torch.no_grad():
+        return await _run_plan_async(
+            _prefill_plan(workers, input_ids, operation_id, attempt_id, cache_key), workers)
 
 
 async def pipeline_decode_step_async(
@@ -381,93 +465,12 @@ async def pipeline_decode_step_async(
     attempt_id: str = "a0",
     cache_key: str | None = None,
 ) -> torch.Tensor:
-    if next_token.ndim != 2 or next_token.shape[0] < 1 or next_token.shape[1] < 1:
-        raise ValueError("next_token must have shape [batch, sequence] with sequence >= 1")
-    if not workers:
-        raise ValueError("workers must not be empty")
-    batch_size, query_len = next_token.shape
-    max_positions = _max_positions(workers[0])
-    lengths = [int(await _async_stage_call(w, "kv_cache_length", cache_key)) for w in workers]
-    cache_lengths = _checked_lengths(
-        lengths, query_len, max_positions, "pipeline_decode_step_async", "pipeline_prefill_async"
-    )
-    hidden = None
-    try:
-        for index, worker in enumerate(workers):
-            kv_len = cache_lengths[index]
-            position_ids = torch.arange(
-                kv_len, kv_len + query_len, dtype=torch.long, device=next_token.device
-            ).unsqueeze(0).expand(batch_size, -1)
-            result = await _async_stage_call(
-                worker, "forward_inference", hidden,
-                input_ids=next_token if index == 0 else None, position_ids=position_ids,
-                operation_id=operation_id, attempt_id=attempt_id, reset_kv=False, cache_key=cache_key,
-            )
-            hidden = result.output
-    except BaseException:
-        await _restore_kv_lengths_async_best_effort(workers, cache_lengths, cache_key)
-        raise
-    assert hidden is not None
-    return hidden
-
-
-async def _async_stage_call(worker: Any, method_name: str, *args: Any, **kwargs: Any) -> Any:
-    """Run a synchronous stage method in a thread; on cancellation wait for it
-    to finish before propagating, so cleanup never races a running call."""
-    method = getattr(worker, method_name)
-    if inspect.iscoroutinefunction(method):
-        return await method(*args, **kwargs)
-    task = asyncio.create_task(asyncio.to_thread(method, *args, **kwargs))
-    try:
-        return await asyncio.shield(task)
-    except asyncio.CancelledError:
-        try:
-            await asyncio.shield(task)
-        except BaseException:
-            pass
-        raise
-
-
-def _clear_kv_best_effort(workers: Sequence[Any], cache_key: str | None) -> None:
-    for worker in workers:
-        try:
-            worker.clear_kv(cache_key)
-        except Exception as exc:
-            log.warning("could not roll back stage KV cache: %s", exc)
-
-
-def _restore_kv_lengths_best_effort(
-    workers: Sequence[Any], lengths: Sequence[int], cache_key: str | None
-) -> None:
-    for worker, length in zip(workers, lengths):
-        try:
-            if length == 0:
-                worker.clear_kv(cache_key)
-            else:
-                worker.trim_kv(length, cache_key)
-        except Exception as exc:
-            log.warning("could not roll back stage KV cache to %d: %s", length, exc)
-
-
-async def _clear_kv_async_best_effort(workers: Sequence[Any], cache_key: str | None) -> None:
-    for worker in workers:
-        try:
-            await _async_stage_call(worker, "clear_kv", cache_key)
-        except Exception as exc:
-            log.warning("could not roll back remote stage KV cache: %s", exc)
-
-
-async def _restore_kv_lengths_async_best_effort(
-    workers: Sequence[Any], lengths: Sequence[int], cache_key: str | None
-) -> None:
-    for worker, length in zip(workers, lengths):
-        try:
-            if length == 0:
-                await _async_stage_call(worker, "clear_kv", cache_key)
-            else:
-                await _async_stage_call(worker, "trim_kv", length, cache_key)
-        except Exception as exc:
-            log.warning("could not roll back remote stage KV cache to %d: %s", length, exc)
+    """``pipeline_decode_step`` for local or remote (coroutine) stages."""
+    with torch.no_grad():
+        return await _run_plan_async(
+            _decode_plan(workers, next_token, operation_id, attempt_id, cache_key,
+                         names=("pipeline_decode_step_async", "pipeline_prefill_async")),
+            workers)
 
 
 __all__ = [
@@ -476,6 +479,8 @@ __all__ = [
     "from_reference_workers",
     "pipeline_prefill",
     "pipeline_decode_step",
+    "pipeline_decode_multi",
+    "pipeline_decode_greedy",
     "pipeline_prefill_async",
     "pipeline_decode_step_async",
 ]

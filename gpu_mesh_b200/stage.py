@@ -11,7 +11,7 @@ runs in the library's CUDA kernels.
 from __future__ import annotations
 
 import ctypes
-from typing import Any
+from typing import Any, NamedTuple
 
 import torch
 
@@ -28,6 +28,20 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class _DeviceArray:
+    """A device pointer as ``__cuda_array_interface__`` (torch wraps it without a copy)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str) -> None:
+        self.__cuda_array_interface__ = {
+            "shape": tuple(shape), "typestr": typestr, "data": (ptr, False), "version": 3, "strides": None,
+        }
+
+
+class _LoadResult(NamedTuple):
+    missing_keys: list[str]
+    unexpected_keys: list[str]
 
 
 class B200Stage:
@@ -426,6 +440,84 @@ class B200Stage:
     def check_device(self) -> None:
         """Raise if a kernel clamped an out-of-range id or position since the last check."""
         _lib.check(self._lib.mg_stage_check_device(self.handle, _stream(self.device)))
+
+    # ------------------------------------------------------------------
+    # Parameters: views of the stage's HBM arena under the reference's names
+    # ------------------------------------------------------------------
+    def _weight_view(self, which: int, layer: int, shape: tuple[int, ...], row0: int = 0) -> torch.Tensor | None:
+        ptr = ctypes.c_void_p()
+        _lib.check(self._lib.mg_stage_weight(self.handle, which, layer, ctypes.byref(ptr)))
+        if not ptr.value:
+            return None
+        esz = torch.empty((), dtype=self.dtype).element_size()
+        typestr = {4: "<f4", 2: "<i2"}[esz]
+        cols = shape[1] if len(shape) == 2 else 1
+        arr = _DeviceArray(ptr.value + row0 * cols * esz, shape, typestr)
+        t = torch.as_tensor(arr, device=self.device)
+        return t if t.dtype == self.dtype else t.view(self.dtype)
+
+    def named_parameters(self):
+        """(reference name, tensor) for every weight, like LlamaStage's
+        nn.Module parameters (llama_dense.py:293-348; Qwen3Stage adds q_norm /
+        k_norm).  The tensors are views of the stage's own HBM copy: writing
+        them changes the stage, and they are invalid after ``close()``."""
+        cfg = self.cfg
+        H, I, D, V = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim, cfg.vocab_size
+        nq, nkv = cfg.num_attention_heads * D, cfg.num_key_value_heads * D
+        W = _lib
+        if self.has_embedding:
+            yield "embed_tokens.weight", self._weight_view(W.MG_W_EMBED, 0, (V, H))
+        for i in range(self.layer_end - self.layer_start):
+            p = f"layers.{i}."
+            yield p + "self_attn.q_proj.weight", self._weight_view(W.MG_W_QKV, i, (nq, H))
+            yield p + "self_attn.k_proj.weight", self._weight_view(W.MG_W_QKV, i, (nkv, H), nq)
+            yield p + "self_attn.v_proj.weight", self._weight_view(W.MG_W_QKV, i, (nkv, H), nq + nkv)
+            yield p + "self_attn.o_proj.weight", self._weight_view(W.MG_W_O, i, (H, nq))
+            if cfg.qk_norm:
+                yield p + "self_attn.q_norm.weight", self._weight_view(W.MG_W_Q_NORM, i, (D,))
+                yield p + "self_attn.k_norm.weight", self._weight_view(W.MG_W_K_NORM, i, (D,))
+            yield p + "mlp.gate_proj.weight", self._weight_view(W.MG_W_GATE_UP, i, (I, H))
+            yield p + "mlp.up_proj.weight", self._weight_view(W.MG_W_GATE_UP, i, (I, H), I)
+            yield p + "mlp.down_proj.weight", self._weight_view(W.MG_W_DOWN, i, (H, I))
+            yield p + "input_layernorm.weight", self._weight_view(W.MG_W_INPUT_NORM, i, (H,))
+            yield p + "post_attention_layernorm.weight", self._weight_view(W.MG_W_POST_NORM, i, (H,))
+        if self.has_lm_head:
+            yield "norm.weight", self._weight_view(W.MG_W_NORM, 0, (H,))
+            head = self._weight_view(W.MG_W_LM_HEAD, 0, (V, H))
+            embed = self._weight_view(W.MG_W_EMBED, 0, (V, H)) if self.has_embedding else None
+            if embed is None or head.data_ptr() != embed.data_ptr():  # a tied head is listed once
+                yield "lm_head.weight", head
+
+    def parameters(self):
+        for _, t in self.named_parameters():
+            yield t
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        """Every weight under its reference name (a tied head under both names)."""
+        out = dict(self.named_parameters())
+        if self.has_lm_head and "lm_head.weight" not in out:
+            out["lm_head.weight"] = out["embed_tokens.weight"]
+        return out
+
+    def load_state_dict(self, state_dict: dict[str, torch.Tensor], strict: bool = True):
+        """Copy weights into the stage (on its stream); torch's return value and
+        ``strict`` semantics.  Buffers the reference does not persist (RoPE
+        tables) are ignored."""
+        own = self.state_dict()
+        unexpected = [k for k in state_dict if k not in own and "rope" not in k and "rotary" not in k]
+        missing = [k for k in own if k not in state_dict]
+        if strict and (missing or unexpected):
+            raise RuntimeError(f"Error(s) in loading state_dict for B200Stage: missing keys {missing}, "
+                               f"unexpected keys {unexpected}")
+        with torch.no_grad(), torch.cuda.device(self.device):
+            for k, dst in own.items():
+                if k in state_dict:
+                    src = state_dict[k]
+                    if tuple(src.shape) != tuple(dst.shape):
+                        raise RuntimeError(f"size mismatch for {k}: copying a param with shape "
+                                           f"{tuple(src.shape)}, the stage has {tuple(dst.shape)}")
+                    dst.copy_(src.detach().to(device=self.device, dtype=self.dtype))
+        return _LoadResult(missing, unexpected)
 
     # Reference-compatible cache helpers (Qwen3Stage.cache_length / trim_cache,
     # models/qwen3_hf.py:310-331), keyed by slot.

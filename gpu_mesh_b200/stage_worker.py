@@ -17,7 +17,7 @@ from typing import Any
 import torch
 
 from gpu_mesh_b200.stage import B200Stage
-from gpu_mesh_b200.transport import move_boundary
+from gpu_mesh_b200.boundary import move_to_stage
 
 
 @dataclass
@@ -203,6 +203,14 @@ class B200StageWorker:
                 if cache_key is not None:
                     del self._slots[cache_key]
 
+    @property
+    def _kv_caches_by_key(self) -> dict[str | None, KVSlotRef]:
+        """The named request contexts this stage holds, as the reference
+        worker's dict of the same name lists them (stage_worker.py:112-116,
+        358-381; the unnamed default context is not in it)."""
+        with self._inference_lock:
+            return {k: KVSlotRef(self._model, s) for k, s in self._slots.items() if k is not None}
+
     def clear_all_kv(self) -> None:
         with self._inference_lock:
             self._model.kv_free_all()
@@ -255,7 +263,7 @@ class B200StageWorker:
 
     # ------------------------------------------------------------------
     def _move_input(self, hidden: torch.Tensor) -> torch.Tensor:
-        return move_boundary(hidden, self._ctx.device, transport=self._ctx.transport)
+        return move_to_stage(hidden, self._ctx.device, transport=self._ctx.transport)
 
     def _boundary_output(self, output: torch.Tensor) -> torch.Tensor:
         """Detached output; CPU for transport "cpu" (stage_worker.py:436-442)."""

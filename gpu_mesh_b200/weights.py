@@ -13,6 +13,7 @@ the same slice generated as part of the whole model, on any host.
 """
 from __future__ import annotations
 
+import os
 import zlib
 from collections.abc import Iterator
 
@@ -92,6 +93,136 @@ def synthetic_tensor(
     return t.to(dtype)
 
 
+# ---------------------------------------------------------------------------
+# Device-independent N(0, std) weights
+# ---------------------------------------------------------------------------
+# torch's CPU and CUDA generators draw different normal streams, and drawing
+# billions of normals on a host takes minutes.  The "portable" weights are a
+# pure function of (seed, tensor name, element index) in integer arithmetic:
+# a bijective 32-bit hash of the index picks one of 65536 equiprobable normal
+# quantiles, so the same tensor comes out bit-identical on any host or GPU, and
+# a GPU draws a whole model in well under a second.  The hash is two rounds of
+# a xorshift-multiply finalizer (constants from Wellons' hash-prospector
+# search); every step is a bijection mod 2^32.
+
+_M32 = 0xFFFFFFFF
+_MUL1, _MUL2 = 0x21F0AAAD, 0x735A2D97
+_QUANTILES = 65536
+_CHUNK = 1 << 24
+
+
+def _portable_keys(seed: int, global_key: str) -> tuple[int, int]:
+    h = zlib.crc32(global_key.encode())
+    return (h + seed * 0x9E3779B9) & _M32, zlib.crc32(f"{seed}/{global_key}".encode()) & _M32
+
+
+def _quantile_table(std: float, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    p = (torch.arange(_QUANTILES, dtype=torch.float64) + 0.5) / _QUANTILES
+    return (torch.special.ndtri(p) * std).to(torch.float32).to(dtype).to(device)
+
+
+def _mix_torch(x: torch.Tensor) -> torch.Tensor:
+    # int64 holding values < 2^32; constants < 2^31, so products stay < 2^63
+    x = x ^ (x >> 16)
+    x = (x * _MUL1) & _M32
+    x = x ^ (x >> 15)
+    x = (x * _MUL2) & _M32
+    return x ^ (x >> 15)
+
+
+def _mix_numpy(x, tmp) -> None:
+    import numpy as np
+
+    np.right_shift(x, 16, out=tmp)
+    x ^= tmp
+    x *= np.uint32(_MUL1)  # uint32 arithmetic wraps mod 2^32
+    np.right_shift(x, 15, out=tmp)
+    x ^= tmp
+    x *= np.uint32(_MUL2)
+    np.right_shift(x, 15, out=tmp)
+    x ^= tmp
+
+
+def _portable_index_torch(n: int, k1: int, k2: int, device: torch.device) -> Iterator[tuple[int, torch.Tensor]]:
+    for s in range(0, n, _CHUNK):
+        m = min(_CHUNK, n - s)
+        x = (torch.arange(s, s + m, dtype=torch.int64, device=device) + k1) & _M32
+        yield s, _mix_torch(_mix_torch(x) ^ k2) >> 16
+
+
+def _portable_cpu(n: int, k1: int, k2: int, table_bits):
+    """Hash and table lookup in numpy uint32 arithmetic, chunks spread over threads."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    out = np.empty(n, dtype=table_bits.dtype)
+    step, per_task = 1 << 18, 1 << 22
+
+    def run(lo: int) -> None:
+        x = np.empty(step, dtype=np.uint32)
+        tmp = np.empty(step, dtype=np.uint32)
+        base = np.arange(step, dtype=np.uint32)
+        for s in range(lo, min(lo + per_task, n), step):
+            m = min(step, n - s, lo + per_task - s)
+            np.add(base[:m], np.uint32((s + k1) & _M32), out=x[:m])
+            _mix_numpy(x[:m], tmp[:m])
+            x[:m] ^= np.uint32(k2)
+            _mix_numpy(x[:m], tmp[:m])
+            np.right_shift(x[:m], 16, out=tmp[:m])
+            np.take(table_bits, tmp[:m], out=out[s : s + m])
+
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+        list(pool.map(run, range(0, n, per_task)))
+    return out
+
+
+def portable_quantile_index(n: int, seed: int, global_key: str, device: torch.device | str = "cpu") -> torch.Tensor:
+    """The 16-bit quantile index of elements 0..n-1 of a tensor (int64 [n])."""
+    device = torch.device(device)
+    if n >= 1 << 32:
+        raise ValueError("portable weights cover tensors of fewer than 2^32 elements")
+    k1, k2 = _portable_keys(seed, global_key)
+    if device.type == "cpu":
+        import numpy as np
+
+        return torch.from_numpy(_portable_cpu(n, k1, k2, np.arange(_QUANTILES, dtype=np.int64)))
+    out = torch.empty(n, dtype=torch.int64, device=device)
+    for s, idx in _portable_index_torch(n, k1, k2, device):
+        out[s : s + idx.numel()] = idx
+    return out
+
+
+def portable_tensor(
+    global_key: str,
+    shape: tuple[int, ...],
+    *,
+    seed: int = 0,
+    dtype: torch.dtype = torch.float32,
+    device: torch.device | str = "cpu",
+    std: float = 0.02,
+) -> torch.Tensor:
+    """N(0, std) weights (norm vectors one) that are bit-identical on every device."""
+    device = torch.device(device)
+    if len(shape) == 1:
+        return torch.ones(shape, dtype=dtype, device=device)
+    n = 1
+    for d in shape:
+        n *= d
+    if n >= 1 << 32:
+        raise ValueError("portable weights cover tensors of fewer than 2^32 elements")
+    k1, k2 = _portable_keys(seed, global_key)
+    table = _quantile_table(std, dtype, torch.device("cpu"))
+    if device.type == "cpu":
+        bits = {2: torch.int16, 4: torch.int32, 8: torch.int64}[table.element_size()]
+        got = _portable_cpu(n, k1, k2, table.view(bits).numpy())
+        return torch.from_numpy(got).view(dtype).view(shape)
+    table = table.to(device)
+    out = torch.empty(n, dtype=dtype, device=device)
+    for s, idx in _portable_index_torch(n, k1, k2, device):
+        out[s : s + idx.numel()] = table[idx]
+    return out.view(shape)
+
+
 def synthetic_stage_state(
     cfg: LlamaConfig,
     layer_start: int,
@@ -102,24 +233,34 @@ def synthetic_stage_state(
     seed: int = 0,
     dtype: torch.dtype = torch.float32,
     device: torch.device | str = "cpu",
+    method: str = "normal",
 ) -> dict[str, torch.Tensor]:
-    """Seeded synthetic weights of one stage, with the stage's local key names."""
+    """Seeded synthetic weights of one stage, with the stage's local key names.
+
+    ``method="normal"`` draws every matrix from torch's generator on
+    ``device``; ``"portable"`` uses the device-independent quantile weights
+    (``portable_tensor``), identical on any host or GPU.
+    """
+    make = {"normal": synthetic_tensor, "portable": portable_tensor}.get(method)
+    if make is None:
+        raise ValueError(f"unknown synthetic weight method {method!r}")
     out: dict[str, torch.Tensor] = {}
     cache: dict[str, torch.Tensor] = {}
     for local, global_key, shape in stage_keys(cfg, layer_start, layer_end, has_embedding, has_lm_head):
         if global_key not in cache:
-            cache[global_key] = synthetic_tensor(global_key, shape, seed=seed, dtype=dtype, device=device)
+            cache[global_key] = make(global_key, shape, seed=seed, dtype=dtype, device=device)
         out[local] = cache[global_key]
     return out
 
 
 def synthetic_model_state(
-    cfg: LlamaConfig, *, seed: int = 0, dtype: torch.dtype = torch.float32, device="cpu"
+    cfg: LlamaConfig, *, seed: int = 0, dtype: torch.dtype = torch.float32, device="cpu",
+    method: str = "normal",
 ) -> dict[str, torch.Tensor]:
     """Whole-model weights with global key names (a one-stage state dict)."""
     return synthetic_stage_state(
         cfg, 0, cfg.num_hidden_layers, has_embedding=True, has_lm_head=True,
-        seed=seed, dtype=dtype, device=device,
+        seed=seed, dtype=dtype, device=device, method=method,
     )
 
 

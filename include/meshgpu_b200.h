@@ -167,6 +167,29 @@ int mg_kv_import(mg_stage* stage, int32_t slot, int32_t local_layer, const void*
 int mg_kv_export(const mg_stage* stage, int32_t slot, int32_t local_layer, void* k, void* v,
                  void* stream);
 
+/* ---- Weights in the stage's HBM arena ---- */
+
+#define MG_W_EMBED 0      /* embed_tokens.weight [V, H] (first stage)                */
+#define MG_W_NORM 1       /* norm.weight [H] (last stage)                             */
+#define MG_W_LM_HEAD 2    /* lm_head.weight [V, H] (last stage; the embedding if tied) */
+#define MG_W_INPUT_NORM 3 /* layers.i.input_layernorm.weight [H]                      */
+#define MG_W_QKV 4        /* layers.i q_proj, k_proj, v_proj rows stacked [(nq+2nkv)D, H] */
+#define MG_W_Q_NORM 5     /* layers.i.self_attn.q_norm.weight [D] (Qwen3)             */
+#define MG_W_K_NORM 6     /* layers.i.self_attn.k_norm.weight [D] (Qwen3)             */
+#define MG_W_O 7          /* layers.i.self_attn.o_proj.weight [H, nq D]               */
+#define MG_W_POST_NORM 8  /* layers.i.post_attention_layernorm.weight [H]             */
+#define MG_W_GATE_UP 9    /* layers.i gate_proj then up_proj rows [2I, H]             */
+#define MG_W_DOWN 10      /* layers.i.mlp.down_proj.weight [H, I]                     */
+
+/* Device address of one weight of the stage (row-major, the stage dtype;
+ * NULL where the stage has no such weight).  The fused q/k/v and gate/up
+ * matrices hold the reference's separate matrices as consecutive row blocks,
+ * so each reference parameter is a contiguous slice.  Backs the stage's
+ * named_parameters / state_dict / load_state_dict (LlamaStage is an
+ * nn.Module, llama_dense.py:293; callers read named_parameters,
+ * inference/server.py:458). */
+int mg_stage_weight(const mg_stage* stage, int32_t which, int32_t local_layer, void** ptr);
+
 /* ---- Forward ---- */
 
 /* Run the stage for one request slot: embedding (first stage) or hidden
@@ -230,6 +253,15 @@ int mg_linear(int32_t dtype, const void* X, int64_t ldx, const void* W, int32_t 
 /* fp32 scratch elements mg_linear needs for this shape. */
 uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32_t epilogue);
 
+/* Status of the mg_linear / mg_linear_noalloc launches on the current device
+ * since the last check: waits for `stream`, then returns MG_EDEVICE if a
+ * launch gave up waiting for its data (a bounded wait of about 2 s ran out;
+ * that launch's Y is invalid), and clears the status.  The launches
+ * themselves return as soon as they are queued, so they cannot report it.
+ * Instrumentation of this library's own kernels; no counterpart in the
+ * reference. */
+int mg_linear_check_device(void* stream);
+
 /* The same linear layer as mg_linear, for callers that cannot allocate
  * device memory: a process whose device memory is owned by another
  * allocator (a serving framework's caching allocator, say) and may not take
@@ -242,9 +274,10 @@ uint64_t mg_linear_scratch(int32_t dtype, int32_t M, int32_t N, int32_t K, int32
  * fp32 elements, 4 MiB), present on every GPU that loads the library until
  * the process exits.  That covers the decode layers of the benchmark models
  * up to 16 token rows; a shape whose split-K needs more fails with MG_EINVAL
- * and says how much it needs.  The first call on a device looks up
- * that device's copy of the array, so make the first call (per device) before
- * any stream capture.  All calls on one device within a process share the
+ * and says how much it needs.  Each call looks up the current device's copy of
+ * the array (the lookup during a stream capture reuses the previous call's
+ * address), so make one call per device before any stream capture.  A bounded
+ * wait that runs out is reported by mg_linear_check_device.  All calls on one device within a process share the
  * array and leave their partial sums in it; the tile counters at its front
  * must start at zero, so every call clears them first (an asynchronous
  * memset on `stream`, no allocation).  Two calls that overlap on the GPU,
@@ -279,6 +312,24 @@ int mg_stage_profile_read(mg_stage* stage, mg_profile* out);
 
 /* Kernels launched by this library in this process so far. */
 uint64_t mg_launch_count(void);
+
+/* ---- Stage boundaries between GPUs of one process ----
+ * Replace the reference's move_boundary / probe_cuda_path
+ * (transport/local_cuda.py:27-90), which moves a stage output with
+ * Tensor.to on the caller's stream: here the copy is queued on a side stream
+ * of the caller's choosing, ordered by events, into a buffer the receiving
+ * stage owns. */
+
+/* Let `device` read and write `peer`'s memory over NVLink (every B200 pair on
+ * an NVSwitch box).  *enabled = 1 if the pair has peer access (now enabled),
+ * 0 if copies between them must stage through host memory. */
+int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled);
+
+/* Queue a copy of `bytes` from `src` on `src_device` to `dst` on `dst_device`
+ * on `stream` (cudaMemcpyPeerAsync: direct over NVLink when peer access is
+ * enabled). */
+int mg_peer_copy(void* dst, int32_t dst_device, const void* src, int32_t src_device, uint64_t bytes,
+                 void* stream);
 
 /* ---- Sampling (inference/sampling.py) ---- */
 

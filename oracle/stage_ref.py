@@ -162,7 +162,10 @@ class OracleStage:
         c = self.caches.get(key)
         return 0 if not c else int(c[0][0].shape[2])
 
-    def forward(self, x=None, *, input_ids=None, position_ids=None, key=None, use_cache=True):
+    def forward(self, x=None, *, input_ids=None, position_ids=None, key=None, use_cache=True,
+                last_only=False):
+        """``last_only`` applies the final norm and lm_head to the last position
+        only (the prefill logits a sampler reads); the layers see every position."""
         cfg = self.cfg
         if self.has_embedding:
             B, S = input_ids.shape
@@ -187,6 +190,8 @@ class OracleStage:
         if use_cache:
             self.caches[key] = new
         if self.has_lm_head:
+            if last_only:
+                x = x[:, -1:]
             x = linear(rms_norm(x, self.state["norm.weight"], cfg.rms_norm_eps), self.state["lm_head.weight"])
         return x
 
@@ -232,13 +237,13 @@ def build_stages(cfg, n_stages: int, full_state: dict, dtype=torch.float32, rang
     return stages
 
 
-def prefill(stages: list[OracleStage], input_ids: torch.Tensor, key=None) -> torch.Tensor:
+def prefill(stages: list[OracleStage], input_ids: torch.Tensor, key=None, last_only=False) -> torch.Tensor:
     """pipeline_prefill (pipeline.py:110-163): clear, then stages in order."""
     for s in stages:
         s.clear(key)
     h = None
     for i, s in enumerate(stages):
-        h = s.forward(h, input_ids=input_ids if i == 0 else None, key=key)
+        h = s.forward(h, input_ids=input_ids if i == 0 else None, key=key, last_only=last_only)
     return h
 
 
@@ -313,3 +318,24 @@ def top_p_acceptable(logits: torch.Tensor, temperature: float, top_p: float, u: 
         hit = keep & (inc > u - eps) & (exc <= u + eps)
         out.update(si[hit].tolist())
     return out
+
+
+def exact_bar(got: torch.Tensor, ref: torch.Tensor, exact: torch.Tensor, what: str = "") -> dict:
+    """The bf16 parity bar at full model width, where north of 2e-2 max-abs is
+    the reference's own rounding noise: the implementation under test must be
+    no further from the exactly-rounded computation (``exact_rounding``) than
+    the reference's bf16 arithmetic (this oracle, or the reference itself) is:
+
+        mean |got - exact| <= 1.5 * mean |ref - exact| + 1e-3
+        max  |got - exact| <= max(2e-2, 2 * max |ref - exact|)
+
+    Raises AssertionError with the figures; returns them otherwise."""
+    e_got, e_ref = (got.float() - exact.float()).abs(), (ref.float() - exact.float()).abs()
+    stats = {
+        "mean_got": float(e_got.mean()), "mean_ref": float(e_ref.mean()),
+        "max_got": float(e_got.max()), "max_ref": float(e_ref.max()),
+        "max_got_vs_ref": float((got.float() - ref.float()).abs().max()),
+    }
+    assert stats["mean_got"] <= 1.5 * stats["mean_ref"] + 1e-3, (what, stats)
+    assert stats["max_got"] <= max(2e-2, 2 * stats["max_ref"]), (what, stats)
+    return stats

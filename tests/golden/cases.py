@@ -108,3 +108,84 @@ def sketch(logits: torch.Tensor) -> dict[str, torch.Tensor]:
         "mean": x.mean(-1),
         "std": x.std(-1),
     }
+
+
+# ---------------------------------------------------------------------------
+# Whole models at the benchmark geometries, bf16, with the device-independent
+# ("portable") synthetic weights so that a GPU regenerates the identical model
+# in a second.  The reference runs the prompt and a free-running greedy stream;
+# the fixtures keep the tokens, every step's top logits and a fixed subsample
+# of the vocabulary, and the same logits from the oracle under float64
+# accumulation (teacher-forced on the reference's tokens), which measures the
+# reference's own rounding noise.
+# ---------------------------------------------------------------------------
+
+MODEL_SUB_STRIDE = 997  # logits[..., ::997] per row and step
+MODEL_TOPK = 8
+
+
+@dataclass
+class ModelCase:
+    name: str
+    arch: str
+    cfg: dict
+    stages: int
+    batch: int
+    prompt: int
+    steps: int
+    seed: int = 0
+    dtype: torch.dtype = torch.bfloat16
+
+    def config(self) -> LlamaConfig:
+        if self.arch == "qwen3":
+            return LlamaConfig(**self.cfg, qk_norm=True, mask_policy="cache")
+        return LlamaConfig(**self.cfg)
+
+    def prompt_ids(self) -> torch.Tensor:
+        g = torch.Generator().manual_seed(5000 + self.seed)
+        return torch.randint(0, self.cfg["vocab_size"], (self.batch, self.prompt), generator=g)
+
+
+# Llama-3-8B: one 8-row micro-batch of the decode benchmark, its 1024-token prompts.
+LLAMA3_8B = ModelCase(
+    name="model_llama3_8b_bf16",
+    arch="llama",
+    cfg=dict(
+        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=2048,
+        rms_norm_eps=1e-5, rope_theta=500000.0,
+    ),
+    stages=2, batch=8, prompt=1024, steps=32,
+)
+
+# TinyLlama-1.1B: batch 8, 512-token prompts, 2 stages.
+TINYLLAMA_1B = ModelCase(
+    name="model_tinyllama_1b_bf16",
+    arch="llama",
+    cfg=dict(
+        vocab_size=32000, hidden_size=2048, intermediate_size=5632, num_hidden_layers=22,
+        num_attention_heads=32, num_key_value_heads=4, head_dim=64, max_position_embeddings=2048,
+        rms_norm_eps=1e-5, rope_theta=10000.0,
+    ),
+    stages=2, batch=8, prompt=512, steps=32,
+)
+
+# Qwen3-4B: QK-norm, tied embeddings, theta 1e6; 2048-token prompts (4 rows).
+QWEN3_4B = ModelCase(
+    name="model_qwen3_4b_bf16",
+    arch="qwen3",
+    cfg=dict(
+        vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=36,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=4096,
+        rms_norm_eps=1e-6, rope_theta=1_000_000.0, tie_word_embeddings=True,
+    ),
+    stages=2, batch=4, prompt=2048, steps=32,
+)
+
+MODEL_CASES = [LLAMA3_8B, TINYLLAMA_1B, QWEN3_4B]
+
+
+def model_indices(top_i: torch.Tensor, vocab: int) -> torch.Tensor:
+    """Vocabulary indices kept per row: the reference's top-k, then the fixed subsample."""
+    sub = torch.arange(0, vocab, MODEL_SUB_STRIDE).expand(*top_i.shape[:-1], -1)
+    return torch.cat([top_i, sub], dim=-1)

@@ -1,9 +1,8 @@
 """Generate the golden vectors by running the REFERENCE implementation.
 
-Run in a container that has the reference checkout (hungtrab/gpu_mesh) at
-/root/reference:
+Run where a checkout of the reference (hungtrab/gpu_mesh) is available:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout>
 
 It imports the reference's own portable pipeline (``build_pipeline``,
 ``pipeline_prefill``, ``pipeline_decode_step``, ``LlamaStage``,
@@ -146,7 +145,7 @@ def run_top_p() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of a reference checkout (its src/ is imported)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     torch.set_num_threads(8)

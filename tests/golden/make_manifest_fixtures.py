@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (hungtrab/gpu_mesh):
 
-    python tests/golden/make_manifest_fixtures.py [--reference /root/reference]
+    python tests/golden/make_manifest_fixtures.py --reference <checkout>
 
 The reference's artifact package (``meshgpu.artifacts``) ships only inside
 its source tarball (kaggle/meshgpu-source-20260914/meshgpu-kaggle-smoke.tar.gz),
@@ -162,7 +162,7 @@ def make(name: str, scratch: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of a reference checkout")
     args = ap.parse_args()
     torch.set_num_threads(8)
     OUT.mkdir(exist_ok=True)

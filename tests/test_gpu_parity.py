@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from gpu_mesh_b200 import build_pipeline, pipeline_decode_step, pipeline_prefill
+from gpu_mesh_b200.schedule import MicroBatchPipeline
 from gpu_mesh_b200.weights import synthetic_model_state
 from oracle import stage_ref as R
 from tests.conftest import load_golden
@@ -30,20 +31,29 @@ def tol(dtype, ref: torch.Tensor) -> float:
     return FP32_REL * float(ref.abs().max()) if dtype == torch.float32 else BF16_ABS
 
 
-def build(case, transport="local_cuda"):
+def stage_devices(n_stages: int, gpus: int) -> list[torch.device]:
+    """Stage i on GPU i mod ``gpus``; skips when this host has fewer GPUs."""
+    if torch.cuda.device_count() < gpus:
+        pytest.skip(f"needs {gpus} GPUs")
+    return [torch.device("cuda", i % gpus) for i in range(n_stages)]
+
+
+def build(case, transport="local_cuda", gpus=1):
     cfg = case.config()
     full = synthetic_model_state(cfg, seed=case.seed)
-    dev = torch.device("cuda", 0)
-    workers = build_pipeline(cfg, case.stages, [dev] * case.stages, transport=transport,
+    workers = build_pipeline(cfg, case.stages, stage_devices(case.stages, gpus), transport=transport,
                              dtype=case.dtype, state_dict=full)
     oracle = R.build_stages(cfg, case.stages, full, dtype=case.dtype)
     return workers, oracle
 
 
+@pytest.mark.parametrize("gpus", [1, 2], ids=["one-gpu", "two-gpus"])
 @pytest.mark.parametrize("case", CASES, ids=lambda c: c.name)
-def test_stage_path_matches_reference_and_oracle(case):
+def test_stage_path_matches_reference_and_oracle(case, gpus):
+    """Two stages on one GPU, or on two GPUs with the boundary moved by the
+    side-stream peer copy."""
     g = load_golden(case.name)
-    workers, oracle = build(case)
+    workers, oracle = build(case, gpus=gpus)
     ids = g["prompt"]
     with torch.no_grad():
         got = pipeline_prefill(workers, ids, cache_key="p").float().cpu()
@@ -74,10 +84,11 @@ def test_stage_path_matches_reference_and_oracle(case):
         w.close()
 
 
-def test_c1_free_running_greedy_is_token_identical():
+@pytest.mark.parametrize("gpus", [1, 2], ids=["one-gpu", "two-gpus"])
+def test_c1_free_running_greedy_is_token_identical(gpus):
     """The tiny fp32 Llama case: 32 greedy steps, no teacher forcing."""
     g = load_golden(C1.name)
-    workers, _ = build(C1)
+    workers, _ = build(C1, gpus=gpus)
     with torch.no_grad():
         logits = pipeline_prefill(workers, g["prompt"], cache_key="s", logits="last")
         tok = logits[:, -1].argmax(-1, keepdim=True)
@@ -102,4 +113,45 @@ def test_cpu_transport_matches_local_cuda():
     assert la.device.type == "cpu" and lb.device.type == "cuda"
     assert torch.equal(la, lb.cpu())
     for w in a + b:
+        w.close()
+
+
+@pytest.mark.parametrize("gpus", [1, 2], ids=["one-gpu", "two-gpus"])
+def test_c1_micro_batches_in_flight_reproduce_the_reference_stream(gpus):
+    """MicroBatchPipeline: three contexts of the C1 prompt in flight across
+    the two stages; each must generate the reference's 33-token stream."""
+    g = load_golden(C1.name)
+    workers, _ = build(C1, gpus=gpus)
+    pipe = MicroBatchPipeline(workers)
+    keys = ["m0", "m1", "m2"]
+    out = pipe.generate_greedy([g["prompt"]] * 3, keys, C1.steps + 1)
+    for o in out:
+        assert torch.equal(o, g["tokens"])
+    assert all(w.kv_cache_length(k) == g["prompt"].shape[1] + C1.steps for w in workers for k in keys)
+    for w in workers:
+        w.close()
+
+
+@pytest.mark.parametrize("gpus", [1, 2], ids=["one-gpu", "two-gpus"])
+def test_bf16_micro_batches_match_single_context_decoding(gpus):
+    """The small bf16 case: micro-batches in flight give exactly the tokens of
+    decoding each context alone through pipeline_decode_step (same kernels,
+    same row counts), and match the reference's stream up to a near-tie."""
+    case = CASES[1]
+    g = load_golden(case.name)
+    workers, oracle = build(case, gpus=gpus)
+    pipe = MicroBatchPipeline(workers)
+    prompts = [g["prompt"], g["prompt"].flip(0)]
+    out = pipe.generate_greedy(prompts, ["x", "y"], case.steps + 1)
+    with torch.no_grad():
+        for p, o in zip(prompts, out):
+            logits = pipeline_prefill(workers, p, cache_key="alone", logits="last")
+            tok = logits[:, -1].argmax(-1, keepdim=True)
+            alone = [tok.cpu()]
+            for k in range(case.steps):
+                logits = pipeline_decode_step(workers, tok, operation_id=2 + k, cache_key="alone", logits="last")
+                tok = logits[:, -1].argmax(-1, keepdim=True)
+                alone.append(tok.cpu())
+            assert torch.equal(o, torch.cat(alone, 1))
+    for w in workers:
         w.close()

@@ -210,3 +210,104 @@ def test_async_call_drains_on_cancel():
     asyncio.run(main())
     # the running stage call finished before cancellation propagated
     assert any(c[0] == "fwd" for c in w.calls)
+
+
+class FakeRemoteWorker(FakeWorker):
+    """A stage reached over RPC: coroutine methods, as the reference's remote workers."""
+
+    async def clear_kv(self, key=None):
+        FakeWorker.clear_kv(self, key)
+
+    async def kv_cache_length(self, key=None):
+        return FakeWorker.kv_cache_length(self, key)
+
+    async def trim_kv(self, length, key=None):
+        FakeWorker.trim_kv(self, length, key)
+
+    async def forward_inference(self, hidden, **kw):
+        await asyncio.sleep(0)
+        return FakeWorker.forward_inference(self, hidden, **kw)
+
+
+def test_async_plans_drive_remote_stages_and_roll_back():
+    a, b = FakeRemoteWorker("a"), FakeRemoteWorker("b", fail_on=3)
+
+    async def main():
+        out = await P.pipeline_prefill_async([a, b], torch.zeros(2, 3, dtype=torch.long), cache_key="r")
+        assert out.shape == (2, 3, 4)
+        await P.pipeline_decode_step_async([a, b], torch.zeros(2, 1, dtype=torch.long), operation_id=2,
+                                           cache_key="r")
+        assert a.calls[-1] == ("fwd", "r", [3])
+        with pytest.raises(RuntimeError, match="b failed"):
+            await P.pipeline_decode_step_async([a, b], torch.zeros(2, 1, dtype=torch.long), operation_id=3,
+                                               cache_key="r")
+        with pytest.raises(RuntimeError, match="pipeline_decode_step_async requires a prefilled"):
+            await P.pipeline_decode_step_async([a, b], torch.zeros(1, 1, dtype=torch.long), operation_id=4,
+                                               cache_key="other")
+
+    asyncio.run(main())
+    assert a.len["r"] == 4 and b.len["r"] == 4  # the failed step was trimmed away on both stages
+
+
+def test_cancelled_async_prefill_rolls_back_after_the_drain():
+    gate = threading.Event()
+    a, b = FakeWorker("a"), FakeWorker("b", delay_event=gate)
+
+    async def main():
+        task = asyncio.create_task(P.pipeline_prefill_async([a, b], torch.zeros(1, 2, dtype=torch.long),
+                                                            cache_key="c"))
+        await asyncio.sleep(0.05)
+        task.cancel()
+        await asyncio.sleep(0.05)
+        gate.set()
+        with pytest.raises(asyncio.CancelledError):
+            await task
+
+    asyncio.run(main())
+    assert a.kv_cache_length("c") == 0 and b.kv_cache_length("c") == 0
+
+
+def test_rollback_failures_are_logged_not_raised(caplog):
+    class Stubborn(FakeWorker):
+        def trim_kv(self, length, key=None):
+            raise RuntimeError("cannot trim")
+
+    a, b = Stubborn("a"), FakeWorker("b", fail_on=2)
+    P.pipeline_prefill([a, b], torch.zeros(1, 2, dtype=torch.long), cache_key="s")
+    with pytest.raises(RuntimeError, match="b failed"):
+        P.pipeline_decode_step([a, b], torch.zeros(1, 1, dtype=torch.long), operation_id=2, cache_key="s")
+    assert "rollback step trim_kv failed" in caplog.text
+    assert b.len["s"] == 2
+
+
+def test_portable_weights_are_the_same_on_every_code_path():
+    from gpu_mesh_b200 import weights as W
+
+    n = 1_000_003
+    k1, k2 = W._portable_keys(7, "layers.3.mlp.down_proj.weight")
+    host = W.portable_quantile_index(n, 7, "layers.3.mlp.down_proj.weight")
+    torch_path = torch.cat([i for _, i in W._portable_index_torch(n, k1, k2, torch.device("cpu"))])
+    assert torch.equal(host, torch_path)  # the numpy kernel (hosts) and the torch kernel (GPUs) agree
+    w = W.portable_tensor("layers.3.mlp.down_proj.weight", (1000, 1000), seed=7, dtype=torch.bfloat16)
+    table = W._quantile_table(0.02, torch.bfloat16, torch.device("cpu"))
+    assert torch.equal(w.flatten(), table[host[:1_000_000]])
+    assert abs(float(w.float().std()) - 0.02) < 2e-4 and abs(float(w.float().mean())) < 2e-4
+    again = W.portable_tensor("layers.3.mlp.down_proj.weight", (1000, 1000), seed=7, dtype=torch.bfloat16)
+    other = W.portable_tensor("layers.3.mlp.down_proj.weight", (1000, 1000), seed=8, dtype=torch.bfloat16)
+    assert torch.equal(w, again) and not torch.equal(w, other)
+    cfg = LlamaConfig(**TINY)
+    full = synthetic_model_state(cfg, seed=1, method="portable")
+    stage = synthetic_stage_state(cfg, 2, 4, has_embedding=False, has_lm_head=True, seed=1, method="portable")
+    assert torch.equal(stage["layers.0.self_attn.q_proj.weight"], full["layers.2.self_attn.q_proj.weight"])
+    with pytest.raises(ValueError, match="unknown synthetic weight method"):
+        synthetic_model_state(cfg, method="uniform")
+
+
+def test_boundary_transports_on_the_host():
+    from gpu_mesh_b200.boundary import move_to_stage
+
+    x = torch.arange(6.0).view(1, 2, 3)
+    assert move_to_stage(x, "cpu", transport="cpu") is x
+    assert move_to_stage(x, "cpu", transport="local_cuda") is x
+    with pytest.raises(ValueError, match="unsupported local boundary transport"):
+        move_to_stage(x, "cpu", transport="rdma")
