@@ -518,6 +518,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-weak", action="store_true",
                     help="N > 1: skip the weak-scaling measurement (N groups of 32 rows in flight)")
+    ap.add_argument("--even-split", action="store_true",
+                    help="N > 1: the reference's even layer split instead of ranges that even out the "
+                         "bytes each stage streams")
     ap.add_argument("--no-long-context", action="store_true",
                     help="skip the long-context attention measurement (64 rows x 8192 positions)")
     args = ap.parse_args()

@@ -18,6 +18,7 @@ MG_ESTATE = 2
 MG_ECUDA = 3
 MG_ENOMEM = 4
 MG_EDEVICE = 5
+MG_ETIMEOUT = 6
 
 MG_DTYPE_F32 = 0
 MG_DTYPE_BF16 = 1
@@ -151,6 +152,10 @@ class DeviceRangeError(ValueError):
     """A kernel met an out-of-range token id or position (reported lazily)."""
 
 
+class DeviceTimeoutError(MeshGpuError):
+    """A kernel gave up a bounded wait; the outputs since the last check are invalid."""
+
+
 def lib() -> ctypes.CDLL:
     """Load the stage library once; raise if it has not been built."""
     global _LIB
@@ -185,6 +190,8 @@ def check(status: int) -> None:
         raise RuntimeError(msg)
     if status == MG_EDEVICE:
         raise DeviceRangeError(msg)
+    if status == MG_ETIMEOUT:
+        raise DeviceTimeoutError(msg)
     raise MeshGpuError(msg)
 
 
@@ -194,6 +201,7 @@ SIGNATURES["mg_linear"] = (
 )
 SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i32])
 SIGNATURES["mg_linear_check_device"] = (ctypes.c_int, [_vp])
+SIGNATURES["mg_stage_probe_wait"] = (ctypes.c_int, [_vp, ctypes.c_uint32, _i32, _vp])
 SIGNATURES["mg_stage_weight"] = (ctypes.c_int, [_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)])
 SIGNATURES["mg_peer_access"] = (ctypes.c_int, [_i32, _i32, ctypes.POINTER(ctypes.c_int32)])
 SIGNATURES["mg_peer_copy"] = (ctypes.c_int, [_vp, _i32, _vp, _i32, ctypes.c_uint64, _vp])

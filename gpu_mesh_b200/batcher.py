@@ -1,31 +1,44 @@
-"""Continuous batching over the stage-owned KV (inference/batcher.py of the reference).
+"""Continuous batching over the stage-owned KV cache.
 
-Same public surface as the reference's ``ContinuousBatcher`` (batcher.py:56-426):
+Public surface of the reference's ``ContinuousBatcher``
+(inference/batcher.py:56-426), kept so its callers work unchanged:
 ``start`` / ``stop`` / ``wait_stopped`` / ``submit`` / ``stream`` /
 ``active_count`` / ``pending_count``, the same validation messages, the same
-``SessionResult`` stream (``seq_num`` monotone, ``is_last`` on EOS or
-``max_new_tokens``, ``token_id = -1`` on failure or cancellation) and the same
-cache ownership (one ``seq:<id>`` context per request, cleared on finish,
-failure, cancellation and stop).
+``SessionResult`` stream (``seq_num`` counts tokens from 1, ``is_last`` on EOS
+or ``max_new_tokens``, one ``token_id = -1`` result on failure, cancellation
+or stop) and one ``seq:<id>`` context per request, cleared when it ends.
 
-The decode loop is what changes. The reference decodes its active sequences
-one after another (batcher.py:229-247), each step a full pass over every
-stage's weights for one context. Here one iteration is a single
-``pipeline_decode_multi`` call for all active sequences: every stage reads
-its weights once for the batch, and each row attends to its own context's
-cache at its own length. Sampling follows the reference's ``_sample``
-(session.py:245-259): greedy at temperature 0, else top-p with the request's
-seeded generator. If the batched step fails, the loop retries the step one
-sequence at a time, so a failing context is isolated the way the reference
-isolates it (its own ``-1`` result, its cache cleared).
+The engine is this module's own.  The reference runs its loop as an asyncio
+task that hands each stage call to a thread and decodes its active sequences
+one after another (batcher.py:229-247), a full pass over every weight per
+sequence and token.  Here one engine thread owns every stage call:
+
+* each iteration admits pending requests up to ``max_batch_size`` (one
+  prefill each, its first token sampled from the prefill's last position),
+  then runs ONE batched decode over every active request:
+  ``pipeline_decode_greedy`` when all rows are greedy (the token is chosen
+  inside the last stage's lm_head and only ids leave the GPU), else
+  ``pipeline_decode_multi`` and per-row sampling.  Every request keeps its own
+  KV slot and length; each weight is read once per iteration for all of them;
+* results go to each request's asyncio queue through
+  ``loop.call_soon_threadsafe``; the event loop never blocks on the GPU;
+* a request ends exactly once (``_finish``, under a lock): by EOS or its
+  token budget, by a failure, by its stream being closed, or by ``stop``;
+* if a batched decode fails, every context is rolled back by the pipeline and
+  the iteration is retried one request at a time, so only the failing
+  request ends with ``-1`` (the reference's isolation).
+
+Sampling follows the reference's ``_sample`` (inference/session.py:245-259):
+greedy at temperature 0, else top-p with the request's seeded generator.
 """
 from __future__ import annotations
 
 import asyncio
 import logging
-import time
+import threading
 import uuid
-from dataclasses import dataclass, field
+from collections import deque
+from dataclasses import dataclass
 from typing import Any
 
 import torch
@@ -51,35 +64,37 @@ class SessionResult:
     text: str = ""
 
 
-@dataclass
-class _Sequence:
-    seq_id: str
-    prompt_ids: list[int]
-    sampling: SamplingParams
-    max_new_tokens: int
-    result_queue: asyncio.Queue
-    generator: torch.Generator | None = None
-    generator_device: torch.device | None = None
-    generated: list[int] = field(default_factory=list)
-    seq_num: int = 0
-    finished: bool = False
-    cancelled: bool = False
-    started_at: float = field(default_factory=time.time)
+class _Request:
+    """One request as the engine sees it."""
 
-    def last_token(self) -> int:
-        return self.generated[-1] if self.generated else self.prompt_ids[-1]
+    __slots__ = ("rid", "prompt", "sampling", "budget", "tokens", "queue", "loop", "generator",
+                 "generator_device", "ended", "cancel")
 
-    @property
-    def total_generated(self) -> int:
-        return len(self.generated)
+    def __init__(self, rid: str, prompt: list[int], sampling: SamplingParams, budget: int,
+                 queue: asyncio.Queue, loop: asyncio.AbstractEventLoop) -> None:
+        self.rid = rid
+        self.prompt = prompt
+        self.sampling = sampling
+        self.budget = budget
+        self.tokens: list[int] = []
+        self.queue = queue
+        self.loop = loop
+        self.generator: torch.Generator | None = None
+        self.generator_device: torch.device | None = None
+        self.ended = False     # its terminal result has been queued
+        self.cancel = False    # its stream was closed: end it at the next iteration
 
     @property
-    def cache_key(self) -> str:
-        return f"seq:{self.seq_id}"
+    def key(self) -> str:
+        return f"seq:{self.rid}"
+
+    @property
+    def next_input(self) -> int:
+        return self.tokens[-1] if self.tokens else self.prompt[-1]
 
 
 class ContinuousBatcher:
-    """Drives one batched decode loop across the active sequences.
+    """Batched decode of concurrent requests over shared stage workers.
 
     Usage (as the reference)::
 
@@ -89,6 +104,7 @@ class ContinuousBatcher:
         async for result in batcher.stream(seq_id):
             ...
         batcher.stop()
+        await batcher.wait_stopped()
     """
 
     def __init__(self, workers: list[Any], max_batch_size: int = 8) -> None:
@@ -98,122 +114,105 @@ class ContinuousBatcher:
             raise ValueError("max_batch_size must be positive")
         self._workers = workers
         self._max_batch = max_batch_size
-        self._active: dict[str, _Sequence] = {}
-        self._pending: asyncio.Queue[_Sequence] = asyncio.Queue()
-        self._pending_by_id: dict[str, _Sequence] = {}
-        self._queues: dict[str, asyncio.Queue] = {}
-        self._stream_consumers: set[str] = set()
-        self._lock = asyncio.Lock()
+        self._lock = threading.Lock()
+        self._wake = threading.Condition(self._lock)
+        self._pending: deque[_Request] = deque()
+        self._active: list[_Request] = []
+        self._requests: dict[str, _Request] = {}  # until their stream has read the last result
+        self._streaming: set[str] = set()
+        self._thread: threading.Thread | None = None
+        self._stopped: asyncio.Future | None = None
         self._running = False
-        self._stopping = False
-        self._loop_task: asyncio.Task | None = None
-        self._inflight: set[asyncio.Task] = set()
-        self._op_seq = 0
+        self._op = 0
         self.decode_passes = 0  # batched decode calls made (one weight pass each)
 
-    def _next_op(self) -> int:
-        self._op_seq += 1
-        return self._op_seq
-
     # ------------------------------------------------------------------
-    # Public API (batcher.py:104-219)
+    # Front end (event loop side)
     # ------------------------------------------------------------------
 
     def start(self) -> None:
         if self._running:
             return
-        if self._loop_task is not None and not self._loop_task.done():
+        if self._thread is not None and self._thread.is_alive():
             raise RuntimeError("batcher is still stopping; await wait_stopped() before restarting")
+        loop = asyncio.get_event_loop()
+        self._stopped = loop.create_future()
         self._running = True
-        self._stopping = False
-        self._loop_task = asyncio.ensure_future(self._decode_loop())
+        self._thread = threading.Thread(target=self._engine, args=(loop, self._stopped),
+                                        name="b200-batcher", daemon=True)
+        self._thread.start()
 
     def stop(self) -> None:
-        self._running = False
-        if self._loop_task is not None and not self._loop_task.done():
-            self._stopping = True
-        for seq in list(self._active.values()):
-            if not seq.finished:
-                seq.finished = True
-                seq.cancelled = True
-                seq.result_queue.put_nowait(SessionResult(token_id=-1, seq_num=seq.seq_num, is_last=True))
-        while True:
-            try:
-                seq = self._pending.get_nowait()
-            except asyncio.QueueEmpty:
-                break
-            seq.finished = True
-            seq.cancelled = True
-            self._pending_by_id.pop(seq.seq_id, None)
-            seq.result_queue.put_nowait(SessionResult(token_id=-1, seq_num=seq.seq_num, is_last=True))
-        if self._loop_task:
-            self._loop_task.cancel()
+        """End every pending and active request with a ``-1`` result and let
+        the engine release their contexts and exit."""
+        with self._lock:
+            self._running = False
+            for req in list(self._pending) + self._active:
+                self._finish(req, -1)
+            self._wake.notify_all()
 
     async def wait_stopped(self) -> None:
-        """Wait until a canceled decode loop has drained its worker threads."""
-        task = self._loop_task
-        if task is None:
-            return
-        try:
-            await task
-        except asyncio.CancelledError:
-            pass
+        """Wait until the engine thread has released every context and exited."""
+        if self._stopped is not None:
+            await asyncio.shield(self._stopped)
 
     async def submit(self, prompt_ids: list[int], sampling: SamplingParams, max_new_tokens: int) -> str:
-        """Submit a new request; returns seq_id for streaming."""
+        """Queue a request; returns its seq_id for ``stream``."""
         if not self._running:
             raise RuntimeError("batcher is not running; call start() first")
         if not prompt_ids:
             raise ValueError("prompt_ids must not be empty")
         if max_new_tokens < 1:
             raise ValueError("max_new_tokens must be positive")
-        model_cfg = getattr(getattr(self._workers[0], "_model", None), "cfg", None)
-        vocab_size = getattr(model_cfg, "vocab_size", None)
-        prompt_ids = list(prompt_ids)
-        if vocab_size is not None and any(token < 0 or token >= vocab_size for token in prompt_ids):
+        cfg = getattr(getattr(self._workers[0], "_model", None), "cfg", None)
+        prompt = [int(t) for t in prompt_ids]
+        vocab = getattr(cfg, "vocab_size", None)
+        if vocab is not None and any(t < 0 or t >= vocab for t in prompt):
             raise ValueError("prompt contains an out-of-vocabulary token")
-        max_positions = getattr(model_cfg, "max_position_embeddings", None)
-        if max_positions is not None and len(prompt_ids) + max_new_tokens > max_positions:
+        limit = getattr(cfg, "max_position_embeddings", None)
+        if limit is not None and len(prompt) + max_new_tokens > limit:
             raise ValueError(
-                f"prompt ({len(prompt_ids)}) + max_new_tokens ({max_new_tokens}) "
-                f"exceeds model context {max_positions}"
+                f"prompt ({len(prompt)}) + max_new_tokens ({max_new_tokens}) exceeds model context {limit}"
             )
-        seq_id = uuid.uuid4().hex[:12]
-        q: asyncio.Queue = asyncio.Queue()
-        seq = _Sequence(seq_id=seq_id, prompt_ids=prompt_ids, sampling=sampling,
-                        max_new_tokens=max_new_tokens, result_queue=q)
-        async with self._lock:
+        req = _Request(uuid.uuid4().hex[:12], prompt, sampling, max_new_tokens, asyncio.Queue(),
+                       asyncio.get_running_loop())
+        with self._lock:
             if not self._running:
                 raise RuntimeError("batcher is not running; call start() first")
-            self._queues[seq_id] = q
-            self._pending_by_id[seq_id] = seq
-            await self._pending.put(seq)
-        return seq_id
+            self._requests[req.rid] = req
+            self._pending.append(req)
+            self._wake.notify_all()
+        return req.rid
 
     async def stream(self, seq_id: str):
-        """Async generator: yields SessionResult for each generated token."""
-        q = self._queues.get(seq_id)
-        if q is None:
-            raise RuntimeError(f"seq {seq_id} not found — call submit() first")
-        async with self._lock:
-            if seq_id in self._stream_consumers:
+        """Async generator of the request's SessionResults.  Closing it before
+        the last result cancels the request and releases its context."""
+        with self._lock:
+            req = self._requests.get(seq_id)
+            if req is None:
+                raise RuntimeError(f"seq {seq_id} not found — call submit() first")
+            if seq_id in self._streaming:
                 raise RuntimeError(f"seq {seq_id} already has an active stream consumer")
-            self._stream_consumers.add(seq_id)
-        completed = False
+            self._streaming.add(seq_id)
+        done = False
         try:
             while True:
-                result: SessionResult = await q.get()
+                result: SessionResult = await req.queue.get()
                 yield result
                 if result.is_last:
-                    completed = True
-                    self._queues.pop(seq_id, None)
+                    done = True
                     break
         finally:
-            if not completed:
-                await self._cancel_sequence(seq_id)
-                self._queues.pop(seq_id, None)
-            async with self._lock:
-                self._stream_consumers.discard(seq_id)
+            with self._lock:
+                self._streaming.discard(seq_id)
+                if not done and not req.ended:
+                    req.cancel = True
+                    if req in self._pending:  # never admitted: end it here
+                        self._pending.remove(req)
+                        self._finish(req, -1)
+                    self._wake.notify_all()
+                if req.ended:
+                    self._requests.pop(seq_id, None)
 
     @property
     def active_count(self) -> int:
@@ -221,174 +220,175 @@ class ContinuousBatcher:
 
     @property
     def pending_count(self) -> int:
-        return self._pending.qsize()
+        return len(self._pending)
 
     # ------------------------------------------------------------------
-    # Decode loop
+    # Results
     # ------------------------------------------------------------------
 
-    async def _decode_loop(self) -> None:
-        try:
-            while self._running:
-                await self._admit_pending()
-                if not self._active:
-                    await asyncio.sleep(0.01)
-                    continue
-                batch = [s for s in self._active.values() if not s.finished]
-                if batch:
-                    results = await self._run_sync(self._decode_batch_sync, batch)
-                    for seq, result in zip(batch, results):
-                        if result is not None and not seq.cancelled:
-                            await seq.result_queue.put(result)
-                async with self._lock:
-                    for sid in [sid for sid, s in self._active.items() if s.finished]:
-                        finished_seq = self._active.pop(sid)
-                        self._clear_sequence_cache(finished_seq)
-        finally:
-            try:
-                if self._inflight:
-                    await asyncio.gather(*tuple(self._inflight), return_exceptions=True)
-                for seq in list(self._active.values()):
-                    self._clear_sequence_cache(seq)
-                self._active.clear()
-            finally:
-                self._running = False
-                self._stopping = False
-
-    async def _admit_pending(self) -> None:
-        for _ in range(self._max_batch):
-            async with self._lock:
-                if len(self._active) >= self._max_batch:
-                    break
-                try:
-                    seq = self._pending.get_nowait()
-                except asyncio.QueueEmpty:
-                    break
-                self._pending_by_id.pop(seq.seq_id, None)
-                if seq.cancelled:
-                    continue
-                self._active[seq.seq_id] = seq
-            result = await self._run_sync(self._prefill_sync, seq)
-            if result is not None and not seq.cancelled:
-                await seq.result_queue.put(result)
-
-    async def _cancel_sequence(self, seq_id: str) -> None:
-        async with self._lock:
-            sequence = self._active.get(seq_id) or self._pending_by_id.get(seq_id)
-            if sequence is None:
-                return
-            sequence.cancelled = True
-            sequence.finished = True
-            self._pending_by_id.pop(seq_id, None)
-
-    async def _run_sync(self, function, *args):
-        """Run a blocking stage operation and retain it across cancellation."""
-        task = asyncio.create_task(asyncio.to_thread(function, *args))
-        self._inflight.add(task)
-        task.add_done_callback(self._inflight.discard)
-        try:
-            return await asyncio.shield(task)
-        finally:
-            if task.done():
-                self._inflight.discard(task)
-
-    # ------------------------------------------------------------------
-    # Blocking steps (run in a worker thread)
-    # ------------------------------------------------------------------
-
-    def _sample_row(self, seq: _Sequence, logits: torch.Tensor) -> int:
-        """The reference's ``_sample`` for one row of logits [V]."""
-        if seq.sampling.temperature == 0.0:
-            return int(greedy_sample(logits))
-        return int(top_p_sample(logits, seq.sampling.temperature, seq.sampling.top_p,
-                                generator=self._generator_for(seq, logits)))
-
-    def _advance(self, seq: _Sequence, next_id: int) -> SessionResult:
-        seq.generated.append(next_id)
-        seq.seq_num += 1
-        eos = seq.sampling.eos_token_id
-        is_last = (eos is not None and next_id == eos) or seq.total_generated >= seq.max_new_tokens
-        seq.finished = is_last
-        if is_last:
-            self._clear_sequence_cache(seq)
-        return SessionResult(token_id=next_id, seq_num=seq.seq_num, is_last=is_last)
-
-    def _fail(self, seq: _Sequence, seq_num: int) -> SessionResult:
-        self._clear_sequence_cache(seq)
-        seq.finished = True
-        return SessionResult(token_id=-1, seq_num=seq_num, is_last=True)
-
-    def _prefill_sync(self, seq: _Sequence) -> SessionResult | None:
-        try:
-            input_ids = torch.tensor([seq.prompt_ids], dtype=torch.long)
-            logits = pipeline_prefill(self._workers, input_ids, operation_id=self._next_op(),
-                                      attempt_id=f"pf_{seq.seq_id}", cache_key=seq.cache_key)
-            return self._advance(seq, self._sample_row(seq, logits[0, -1, :]))
-        except Exception:
-            log.exception("prefill failed for seq %s", seq.seq_id)
-            return self._fail(seq, 0)
-
-    def _decode_batch_sync(self, batch: list[_Sequence]) -> list[SessionResult | None]:
-        live = [s for s in batch if not s.finished]
-        if not live:
-            return [None] * len(batch)
-        try:
-            ids = torch.tensor([[s.last_token()] for s in live], dtype=torch.long)
-            keys = [s.cache_key for s in live]
-            greedy = [i for i, s in enumerate(live) if s.sampling.temperature == 0.0]
-            if len(greedy) == len(live) and hasattr(self._workers[-1], "decode_greedy"):
-                # every row greedy: the last stage selects on the device, no logits leave it
-                chosen, _ = pipeline_decode_greedy(self._workers, ids, cache_keys=keys)
-                self.decode_passes += 1
-                out = {id(s): self._advance(s, int(t)) for s, t in zip(live, chosen.tolist())}
-                return [out.get(id(s)) for s in batch]
-            logits = pipeline_decode_multi(self._workers, ids, cache_keys=keys)
-            self.decode_passes += 1
-            tokens: dict[int, int] = {}
-            if greedy:
-                sel = torch.tensor(greedy, device=logits.device)
-                for i, t in zip(greedy, greedy_sample(logits[sel, -1, :]).tolist()):
-                    tokens[i] = int(t)
-            for i, s in enumerate(live):
-                if i not in tokens:
-                    tokens[i] = self._sample_row(s, logits[i, -1, :])
-            out = {id(s): self._advance(s, tokens[i]) for i, s in enumerate(live)}
-        except Exception:
-            log.exception("batched decode failed; retrying %d sequences one by one", len(live))
-            out = {id(s): self._decode_one_sync(s) for s in live}
-        return [out.get(id(s)) for s in batch]
-
-    def _decode_one_sync(self, seq: _Sequence) -> SessionResult | None:
-        if seq.finished:
-            return None
-        try:
-            next_input = torch.tensor([[seq.last_token()]], dtype=torch.long)
-            logits = pipeline_decode_step(self._workers, next_input, operation_id=self._next_op(),
-                                          attempt_id=f"dc_{seq.seq_id}", cache_key=seq.cache_key)
-            return self._advance(seq, self._sample_row(seq, logits[0, -1, :]))
-        except Exception:
-            log.exception("decode failed for seq %s", seq.seq_id)
-            return self._fail(seq, seq.seq_num)
-
-    def _clear_sequence_cache(self, seq: _Sequence) -> None:
-        for worker in self._workers:
-            try:
-                worker.clear_kv(seq.cache_key)
-            except Exception as exc:
-                log.warning("could not clear batcher cache for seq %s on stage: %s", seq.seq_id, exc)
+    def _finish(self, req: _Request, token: int) -> None:
+        """Queue the terminal result of ``req`` once (call with the lock held)."""
+        if req.ended:
+            return
+        req.ended = True
+        self._emit(req, SessionResult(token_id=token, seq_num=len(req.tokens), is_last=True))
 
     @staticmethod
-    def _generator_for(seq: _Sequence, logits: torch.Tensor) -> torch.Generator | None:
-        """One request RNG on the device where its logits are sampled."""
-        if seq.sampling.seed is None:
+    def _emit(req: _Request, result: SessionResult) -> None:
+        try:
+            req.loop.call_soon_threadsafe(req.queue.put_nowait, result)
+        except RuntimeError:  # the event loop has closed; nobody is listening
+            pass
+
+    def _take(self, req: _Request, token: int) -> None:
+        """Record a sampled token; the request ends on EOS or its budget."""
+        with self._lock:
+            if req.ended:
+                return
+            req.tokens.append(token)
+            eos = req.sampling.eos_token_id
+            last = (eos is not None and token == eos) or len(req.tokens) >= req.budget
+            if last:
+                req.ended = True
+            self._emit(req, SessionResult(token_id=token, seq_num=len(req.tokens), is_last=last))
+
+    # ------------------------------------------------------------------
+    # Engine (its own thread; every stage call happens here)
+    # ------------------------------------------------------------------
+
+    def _engine(self, loop: asyncio.AbstractEventLoop, stopped: asyncio.Future) -> None:
+        try:
+            while True:
+                with self._lock:
+                    while self._running and not self._pending and not self._active:
+                        self._wake.wait(timeout=0.05)
+                    if not self._running:
+                        break
+                    room = self._max_batch - len(self._active)
+                    admitted = [self._pending.popleft() for _ in range(min(room, len(self._pending)))]
+                    self._active.extend(admitted)
+                for req in admitted:
+                    if not req.cancel:
+                        self._prefill(req)
+                self._decode([r for r in self._active if not r.ended and not r.cancel and r.tokens])
+                self._retire()
+        except Exception:
+            log.exception("batcher engine failed")
+        finally:
+            with self._lock:
+                self._running = False
+                leftovers = list(self._pending) + self._active
+                self._pending.clear()
+                self._active = []
+                for req in leftovers:
+                    self._finish(req, -1)
+            for req in leftovers:
+                self._release(req)
+            try:
+                loop.call_soon_threadsafe(lambda: stopped.done() or stopped.set_result(None))
+            except RuntimeError:
+                pass
+
+    def _retire(self) -> None:
+        """Drop ended or cancelled requests from the batch and free their contexts."""
+        with self._lock:
+            gone = [r for r in self._active if r.ended or r.cancel]
+            self._active = [r for r in self._active if not (r.ended or r.cancel)]
+            for r in gone:
+                self._finish(r, -1)  # no-op for a request that already ended
+        for r in gone:
+            self._release(r)
+
+    def _release(self, req: _Request) -> None:
+        for w in self._workers:
+            try:
+                w.clear_kv(req.key)
+            except Exception as exc:
+                log.warning("could not clear the context of seq %s: %s", req.rid, exc)
+
+    def _next_op(self) -> int:
+        self._op += 1
+        return self._op
+
+    def _prefill(self, req: _Request) -> None:
+        try:
+            logits = pipeline_prefill(self._workers, torch.tensor([req.prompt], dtype=torch.long),
+                                      operation_id=self._next_op(), attempt_id=f"pf_{req.rid}",
+                                      cache_key=req.key)
+            self._take(req, self._sample(req, logits[0, -1]))
+        except Exception:
+            log.exception("prefill failed for seq %s", req.rid)
+            with self._lock:
+                self._finish(req, -1)
+
+    def _decode(self, batch: list[_Request]) -> None:
+        if not batch:
+            return
+        ids = torch.tensor([[r.next_input] for r in batch], dtype=torch.long)
+        keys = [r.key for r in batch]
+        try:
+            if all(r.sampling.temperature == 0.0 for r in batch) and hasattr(self._workers[-1], "decode_greedy"):
+                chosen, _ = pipeline_decode_greedy(self._workers, ids, cache_keys=keys)
+                self.decode_passes += 1
+                picks = [int(t) for t in chosen.tolist()]
+            else:
+                logits = pipeline_decode_multi(self._workers, ids, cache_keys=keys)
+                self.decode_passes += 1
+                picks = self._sample_rows(batch, logits[:, -1])
+        except Exception:
+            log.exception("batched decode failed; retrying %d requests one at a time", len(batch))
+            for req in batch:
+                self._decode_alone(req)
+            return
+        for req, token in zip(batch, picks):
+            self._take(req, token)
+
+    def _decode_alone(self, req: _Request) -> None:
+        try:
+            logits = pipeline_decode_step(self._workers, torch.tensor([[req.next_input]], dtype=torch.long),
+                                          operation_id=self._next_op(), attempt_id=f"dc_{req.rid}",
+                                          cache_key=req.key)
+            self._take(req, self._sample(req, logits[0, -1]))
+        except Exception:
+            log.exception("decode failed for seq %s", req.rid)
+            with self._lock:
+                self._finish(req, -1)
+
+    # ------------------------------------------------------------------
+    # Sampling
+    # ------------------------------------------------------------------
+
+    def _sample_rows(self, batch: list[_Request], logits: torch.Tensor) -> list[int]:
+        """Greedy rows in one argmax launch, the rest with their own generators."""
+        picks: list[int | None] = [None] * len(batch)
+        greedy = [i for i, r in enumerate(batch) if r.sampling.temperature == 0.0]
+        if greedy:
+            rows = torch.tensor(greedy, device=logits.device)
+            for i, t in zip(greedy, greedy_sample(logits[rows]).tolist()):
+                picks[i] = int(t)
+        for i, r in enumerate(batch):
+            if picks[i] is None:
+                picks[i] = self._sample(r, logits[i])
+        return picks
+
+    def _sample(self, req: _Request, logits: torch.Tensor) -> int:
+        """The reference's ``_sample`` for one row of logits [V]."""
+        if req.sampling.temperature == 0.0:
+            return int(greedy_sample(logits))
+        return int(top_p_sample(logits, req.sampling.temperature, req.sampling.top_p,
+                                generator=self._generator(req, logits.device)))
+
+    @staticmethod
+    def _generator(req: _Request, device: torch.device) -> torch.Generator | None:
+        """One RNG per seeded request, on the device its logits are sampled on."""
+        if req.sampling.seed is None:
             return None
-        device = torch.device(logits.device)
-        if seq.generator is None:
-            seq.generator = make_sampling_generator(seq.sampling, device=device)
-            seq.generator_device = device
-        elif seq.generator_device != device:
+        device = torch.device(device)
+        if req.generator is None:
+            req.generator = make_sampling_generator(req.sampling, device=device)
+            req.generator_device = device
+        elif req.generator_device != device:
             raise RuntimeError(
-                "sampling logits changed device during one sequence: "
-                f"{seq.generator_device} -> {device}"
+                f"sampling logits changed device during one sequence: {req.generator_device} -> {device}"
             )
-        return seq.generator
+        return req.generator

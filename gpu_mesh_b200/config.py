@@ -156,3 +156,41 @@ def split_layers(n_layers: int, n_stages: int) -> list[tuple[int, int]]:
         ranges.append((start, end))
         start = end
     return ranges
+
+
+def balanced_layer_ranges(
+    cfg: "LlamaConfig", n_stages: int, *, rows: int, context: int, bytes_per_elem: int = 2
+) -> list[tuple[int, int]]:
+    """Contiguous layer ranges that even out what each stage streams per decode
+    step, for ``build_pipeline(layer_ranges=...)`` (the planner's ranges in the
+    reference's artifacts, hf_import.py:860-1050, are honoured the same way).
+
+    A layer costs its weights plus the K and V its ``rows`` read at ``context``
+    cached positions; the last stage also streams the lm_head (the embedding
+    is a gather and costs nothing).  The split minimises the largest stage
+    (exact dynamic programme over the contiguous splits)."""
+    L = cfg.num_hidden_layers
+    if n_stages < 1 or n_stages > L:
+        raise ValueError(f"num_stages must be in [1, {L}], got {n_stages}")
+    H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    layer = (H * (nq + 2 * nkv) * D + nq * D * H + 3 * H * I + 2 * rows * context * nkv * D) * bytes_per_elem
+    head = cfg.vocab_size * H * bytes_per_elem
+    inf = float("inf")
+    # best[s][j]: the smallest possible largest stage when stages 0..s-1 hold layers [0, j)
+    best = [[inf] * (L + 1) for _ in range(n_stages + 1)]
+    cut = [[0] * (L + 1) for _ in range(n_stages + 1)]
+    best[0][0] = 0.0
+    for s in range(1, n_stages + 1):
+        for j in range(s, L - (n_stages - s) + 1):
+            for i in range(s - 1, j):
+                cost = (j - i) * layer + (head if s == n_stages else 0)
+                v = max(best[s - 1][i], cost)
+                if v < best[s][j]:
+                    best[s][j], cut[s][j] = v, i
+    ranges, j = [], L
+    for s in range(n_stages, 0, -1):
+        i = cut[s][j]
+        ranges.append((i, j))
+        j = i
+    return ranges[::-1]

@@ -871,8 +871,9 @@ int mg_stage_create(const mg_stage_config* cfg, const mg_stage_weights* w, mg_st
     L.wgu = base + lo[l].wgu;
     L.wd = base + lo[l].wd;
   }
-  if (ce == cudaSuccess) ce = cudaMalloc((void**)&st->err, sizeof(int));
-  if (ce == cudaSuccess) ce = cudaMemset(st->err, 0, sizeof(int));
+  // err[0]: the error word; err[1]: the probe flag of mg_stage_probe_wait
+  if (ce == cudaSuccess) ce = cudaMalloc((void**)&st->err, 2 * sizeof(int));
+  if (ce == cudaSuccess) ce = cudaMemset(st->err, 0, 2 * sizeof(int));
   if (ce != cudaSuccess) {
     if (st->err) cudaFree(st->err);
     cudaFree(st->wbuf);
@@ -1116,6 +1117,18 @@ int mg_stage_weight(const mg_stage* st, int32_t which, int32_t layer, void** ptr
   return MG_OK;
 }
 
+int mg_stage_probe_wait(mg_stage* st, uint32_t limit_us, int32_t flag_set, void* stream) {
+  if (!st) return fail(MG_EINVAL, "null stage");
+  if (limit_us < 1 || limit_us > 2000000u) return fail(MG_EINVAL, "limit_us must be in [1, 2000000]");
+  DeviceGuard guard(st->cfg.device);
+  cudaStream_t s = (cudaStream_t)stream;
+  int* flag = st->err + 1;
+  MG_CUDA(cudaMemsetAsync(flag, flag_set ? 0x01 : 0, sizeof(int), s), "probe flag");
+  MG_LAUNCH(launch_wait_probe(flag, (uint64_t)limit_us * 1000ull, st->err, s), "wait probe");
+  MG_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s), "probe flag reset");
+  return MG_OK;
+}
+
 int mg_stage_check_device(mg_stage* st, void* stream) {
   if (!st) return fail(MG_EINVAL, "null stage");
   DeviceGuard guard(st->cfg.device);
@@ -1134,8 +1147,8 @@ int mg_stage_check_device(mg_stage* st, void* stream) {
     if (st->chain_bar) cudaMemset(st->chain_bar, 0, 64 * sizeof(int));
     st->chain_gen = 0;
     if (st->greedy_best) cudaMemset(st->greedy_best, 0, 64 * sizeof(unsigned long long));
-    return fail(MG_EDEVICE, "a tensor-core kernel timed out waiting for its data; the outputs of "
-                            "the forwards since the last check are invalid");
+    return fail(MG_ETIMEOUT, "a kernel gave up a bounded wait (code 3); the outputs of the "
+                             "forwards since the last check are invalid");
   }
   return fail(MG_EDEVICE, "position_ids contain a value outside [0, %d)",
               st->cfg.max_position_embeddings);
@@ -1253,7 +1266,7 @@ int mg_linear_check_device(void* stream) {
   MG_CUDA(cudaStreamSynchronize((cudaStream_t)stream), "linear error word sync");
   if (h == kErrNone) return MG_OK;
   MG_CUDA(cudaMemset(err, 0, sizeof(int)), "linear error word reset");
-  return fail(MG_EDEVICE, "a linear launch gave up waiting for its data (code %d); its output is invalid", h);
+  return fail(MG_ETIMEOUT, "a linear launch gave up waiting for its data (code %d); its output is invalid", h);
 }
 
 int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled) {

@@ -5,9 +5,17 @@
 // round to the activation dtype, then multiply by the weight in that dtype.
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace mg {
 namespace {
+
+// One thread waits for the stage's probe flag with the bounded wait every
+// kernel of the stage uses; nothing else is in flight, so an expiry leaves
+// nothing behind but code 3 in the error word.
+__global__ void wait_probe_kernel(const int* flag, uint64_t limit_ns, int* err) {
+  if (threadIdx.x == 0) tc::flag_wait(flag, limit_ns, err);
+}
 
 template <typename T>
 __global__ void embed_kernel(const T* __restrict__ table, const int64_t* __restrict__ ids, int H,
@@ -192,6 +200,11 @@ __global__ void kv_copy_kernel(T* __restrict__ kv, int layer, int kvsel, int slo
 }
 
 }  // namespace
+
+cudaError_t launch_wait_probe(const int* flag, uint64_t limit_ns, int* err, cudaStream_t s) {
+  wait_probe_kernel<<<1, 32, 0, s>>>(flag, limit_ns, err);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M, int H, int V,
                          void* out, int* err, cudaStream_t s) {

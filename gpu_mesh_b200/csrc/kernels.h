@@ -193,6 +193,9 @@ struct LinearArgs {
 size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue);
 cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s);
 
+// Bounded wait on `flag` for `limit_ns`; code 3 in `err` on expiry.
+cudaError_t launch_wait_probe(const int* flag, uint64_t limit_ns, int* err, cudaStream_t s);
+
 cudaError_t launch_embed(int dtype, const void* table, const int64_t* ids, int M, int H, int V,
                          void* out, int* err, cudaStream_t s);
 

@@ -62,6 +62,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return true;
 }
 
+// Bounded wait for a flag word that another agent (a CTA, the host) sets to
+// a non-zero value: true once it is set, false (and code 3 in `err`) if it is
+// still zero after `limit_ns` of %globaltimer.
+__device__ __forceinline__ bool flag_wait(const int* flag, uint64_t limit_ns, int* err) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v != 0) return true;
+    if (globaltimer() - t0 > limit_ns) {
+      if (err) atomicCAS(err, 0, kErrTimeout);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int x,
                                             int y) {
   asm volatile(

@@ -10,10 +10,17 @@ point-to-point: the hidden state of a group to the next stage, and the
 sampled token ids from the last stage back to stage 0.
 
 ``decode_loop`` is the schedule.  It is device-agnostic (the compute and
-sampling functions are arguments) so the same code runs on NCCL/GPU in the
-benchmark and on gloo/CPU in the tests.  Hidden states and returning ids
-use two communicators, so the return path never queues behind the forward
-path.
+sampling functions are arguments) so the same code runs on NCCL/GPU and on
+gloo/CPU in the tests.  Hidden states and returning ids use two
+communicators, so the return path never queues behind the forward path.
+
+``PipelineRank`` is the public entry: this process's stage of an N-process
+pipeline, with ``prefill`` and ``decode`` over groups of request contexts in
+flight (greedy inside the last stage's lm_head, or top-p), optional host
+round trips of the sampled ids, and a record of every id the last stage
+produced.  ``verify_one_gpu`` replays a recorded run on one GPU with the
+whole model, teacher-forced on the pipeline's own ids, and reports every
+token where the two differ with the one-GPU top-2 margin there.
 """
 from __future__ import annotations
 
@@ -116,6 +123,183 @@ def decode_loop(
 
 
 # ---------------------------------------------------------------------------
+# One stage of an N-process pipeline
+# ---------------------------------------------------------------------------
+
+class PipelineRank:
+    """This process's pipeline stage (one process per GPU, torch.distributed
+    initialised with one rank per stage).
+
+    ``layer_ranges`` is the split of the model (default: the reference's even
+    split, ``config.split_layers``; ``config.balanced_layer_ranges`` evens
+    out the bytes each stage streams).  Weights are the seeded synthetic ones
+    (``weights.synthetic_stage_state``) unless ``state_dict`` gives this
+    stage's.  ``groups`` is the number of request contexts in flight, each of
+    ``rows`` rows; every stage holds one KV slot per group.
+    """
+
+    def __init__(self, cfg, *, groups: int, rows: int, capacity: int, layer_ranges=None,
+                 dtype: torch.dtype = torch.bfloat16, seed: int = 0, method: str = "portable",
+                 state_dict=None, top_p: tuple[float, float] | None = None, sample_seed: int = 1234) -> None:
+        from gpu_mesh_b200.config import split_layers
+        from gpu_mesh_b200.stage import B200Stage
+        from gpu_mesh_b200.weights import synthetic_stage_state
+
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.ring = Ring(self.rank, self.world)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.cfg = cfg
+        self.ranges = list(layer_ranges or split_layers(cfg.num_hidden_layers, self.world))
+        ls, le = self.ranges[self.rank]
+        first, last = self.ring.first, self.ring.last
+        if state_dict is None:
+            state_dict = synthetic_stage_state(cfg, ls, le, has_embedding=first, has_lm_head=last, seed=seed,
+                                               dtype=dtype, device=self.device, method=method)
+        self.stage = B200Stage(cfg, ls, le, has_embedding=first, has_lm_head=last, device=self.device,
+                               dtype=dtype, state_dict=state_dict)
+        del state_dict
+        torch.cuda.empty_cache()
+        self.dtype = dtype
+        self.groups, self.rows = groups, rows
+        self.slots = list(range(1, groups + 1))
+        for sl in self.slots:
+            self.stage.kv_reserve(sl, rows, capacity)
+        self.top_p = top_p
+        self.sample_gen = torch.Generator(device=self.device).manual_seed(sample_seed)
+        self.ret_group = dist.new_group(list(range(self.world)))
+        self._ids = [torch.empty(rows, 1, dtype=torch.int64, device=self.device) for _ in range(groups)]
+        self._hidden: dict[int, list[torch.Tensor]] = {}
+        self._host = torch.empty(rows, 1, dtype=torch.int64).pin_memory()
+        self.record: list[tuple[int, torch.Tensor]] | None = None  # (group, ids) per last-stage iteration
+
+    def _hidden_bufs(self, S: int) -> list[torch.Tensor]:
+        if S not in self._hidden:
+            self._hidden[S] = [torch.empty(self.rows, S, self.cfg.hidden_size, dtype=self.dtype,
+                                           device=self.device) for _ in range(self.groups)]
+        return self._hidden[S]
+
+    def _tokens(self, out: torch.Tensor) -> torch.Tensor:
+        from gpu_mesh_b200.sampling import greedy_sample, top_p_sample
+
+        if out.dtype == torch.int64:  # already chosen inside the lm_head
+            return out.view(-1, 1)
+        if self.top_p is not None:
+            return top_p_sample(out[:, -1], *self.top_p, generator=self.sample_gen).unsqueeze(-1)
+        return greedy_sample(out[:, -1]).unsqueeze(-1)
+
+    def _run(self, n_steps: int, inputs, forward, S: int, host_tokens: bool):
+        def sample(k, g, out):
+            ids = self._tokens(out).contiguous()
+            if self.record is not None:
+                self.record.append((g, ids.clone()))
+            if host_tokens:  # a server reads every token on the host
+                self._host.copy_(ids, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+                ids = self._host.to(self.device, non_blocking=True)
+            return ids
+
+        bufs = self._hidden_bufs(S)
+        return decode_loop(self.ring, self.groups, n_steps, inputs, forward, sample,
+                           lambda k, g: bufs[g], lambda g: self._ids[g], ret_group=self.ret_group)
+
+    def prefill(self, prompts: list[torch.Tensor] | None, *, host_tokens: bool = False):
+        """One prefill pass of every group's prompt [rows, S] (given on rank 0,
+        None elsewhere; every rank must know S through ``prompt_len``); returns
+        the first sampled ids per group on rank 0."""
+        st = self.stage
+
+        def forward(k, g, x):
+            if self.ring.first:
+                return st.forward_slot(self.slots[g], None, input_ids=x, logits="last", check_values=False)
+            return st.forward_slot(self.slots[g], x, logits="last", check_values=False)
+
+        return self._run(1, prompts, forward, self.prompt_len, host_tokens)
+
+    def decode(self, ids: list[torch.Tensor] | None, n_steps: int, *, host_tokens: bool = False):
+        """``n_steps`` decode steps of every group from ``ids`` (rank 0);
+        returns the last step's ids per group on rank 0."""
+        st = self.stage
+        greedy_inside = self.ring.last and self.top_p is None
+
+        def forward(k, g, x):
+            slot = [self.slots[g]]
+            if greedy_inside:
+                return st.decode_greedy(slot, None if self.ring.first else x,
+                                        input_ids=x if self.ring.first else None)[0]
+            if self.ring.first:
+                return st.decode_multi(slot, None, input_ids=x, logits="last")
+            return st.decode_multi(slot, x, logits="last")
+
+        return self._run(n_steps, ids, forward, 1, host_tokens)
+
+    def reset(self) -> None:
+        for sl in self.slots:
+            self.stage.kv_trim(sl, 0)
+
+    def close(self) -> None:
+        self.stage.close()
+
+    prompt_len: int = 0
+
+
+def verify_one_gpu(cfg, prompts: list[torch.Tensor], record: list[tuple[int, torch.Tensor]], groups: int,
+                   *, dtype: torch.dtype = torch.bfloat16, seed: int = 0, method: str = "portable",
+                   device: torch.device | None = None) -> dict:
+    """Replay a recorded pipeline run with the whole model on one GPU.
+
+    ``record`` is the last stage's ids in iteration order (the prefill's
+    groups, then every decode step's groups).  The replay prefills the same
+    prompts, then decodes every group in ONE pass per step (the one-GPU
+    path: all rows through each weight once), teacher-forced on the
+    pipeline's previous ids so a difference never propagates.  Returns the
+    count of differing tokens and, for each, the one-GPU logit margin between
+    its own choice and the pipeline's."""
+    from gpu_mesh_b200.stage import B200Stage
+    from gpu_mesh_b200.weights import synthetic_stage_state
+
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    L = cfg.num_hidden_layers
+    state = synthetic_stage_state(cfg, 0, L, has_embedding=True, has_lm_head=True, seed=seed, dtype=dtype,
+                                  device=device, method=method)
+    stage = B200Stage(cfg, 0, L, has_embedding=True, has_lm_head=True, device=device, dtype=dtype,
+                      state_dict=state)
+    del state
+    try:
+        rows = prompts[0].shape[0]
+        n_iters = len(record) // groups
+        cap = prompts[0].shape[1] + n_iters + 8
+        slots = list(range(1, groups + 1))
+        for sl in slots:
+            stage.kv_reserve(sl, rows, cap)
+        steps = [[record[k * groups + g][1].view(-1) for g in range(groups)] for k in range(n_iters)]
+        mismatches, margins = 0, []
+        from gpu_mesh_b200.sampling import greedy_sample
+
+        mine = []
+        for g, p in enumerate(prompts):
+            logits = stage.forward_slot(slots[g], None, input_ids=p.to(device), logits="last", check_values=False)
+            mine.append(greedy_sample(logits[:, -1]))
+        compare = [(0, torch.cat(mine), torch.cat(steps[0]), None)]
+        for k in range(1, n_iters):
+            prev = torch.cat(steps[k - 1]).view(-1, 1)
+            ids, logits = stage.decode_greedy(slots, None, input_ids=prev, return_logits=True)
+            compare.append((k, ids, torch.cat(steps[k]), logits[:, -1]))
+        for k, one, pipe, logits in compare:
+            diff = torch.nonzero(one != pipe).flatten().tolist()
+            mismatches += len(diff)
+            for r in diff:
+                m = None if logits is None else float(logits[r, one[r]].float() - logits[r, pipe[r]].float())
+                margins.append({"step": k, "row": r, "one_gpu": int(one[r]), "pipeline": int(pipe[r]),
+                                "margin": m})
+        stage.check_device()
+        return {"tokens_compared": sum(int(c[1].numel()) for c in compare), "token_mismatches": mismatches,
+                "mismatch_margins": margins[:16], "reference": "one GPU, whole model, one pass for all rows, "
+                "teacher-forced on the pipeline's ids"}
+    finally:
+        stage.close()
+
+
+# ---------------------------------------------------------------------------
 # Benchmark on N GPUs (torchrun)
 # ---------------------------------------------------------------------------
 
@@ -123,11 +307,10 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                        traffic: dict | None = None, top_p: tuple[float, float] | None = None) -> None:
     """``top_p`` = (temperature, p): the last stage samples with a seeded device
     generator instead of selecting greedily inside its lm_head."""
-    from gpu_mesh_b200 import greedy_sample
-    from gpu_mesh_b200.sampling import top_p_sample
-    from gpu_mesh_b200.config import split_layers
-    from gpu_mesh_b200.stage import B200Stage
-    from gpu_mesh_b200.weights import synthetic_stage_state
+    from contextlib import nullcontext
+
+    from gpu_mesh_b200.clocks import ClockSampler
+    from gpu_mesh_b200.config import balanced_layer_ranges, split_layers
 
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -138,76 +321,21 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
     ring = Ring(rank, world)
     try:
         hbm, _, peak_kind = peaks
-        ls, le = split_layers(cfg.num_hidden_layers, world)[rank]
-        sd = synthetic_stage_state(cfg, ls, le, has_embedding=ring.first, has_lm_head=ring.last,
-                                   seed=0, dtype=torch.bfloat16, device=dev)
-        stage = B200Stage(cfg, ls, le, has_embedding=ring.first, has_lm_head=ring.last, device=dev,
-                          dtype=torch.bfloat16, state_dict=sd)
-        del sd
-        torch.cuda.empty_cache()
-
         rows_total = args.micro * args.micro_batches
         n_groups = max(world, 1)
         if rows_total % n_groups:
             raise ValueError(f"{rows_total} rows do not split into {n_groups} groups")
         rows = rows_total // n_groups
-        H = cfg.hidden_size
-        slots = list(range(1, n_groups + 1))
+        mean_ctx = args.prompt + args.warmup + args.steps
+        ranges = (split_layers(cfg.num_hidden_layers, world) if getattr(args, "even_split", False) else
+                  balanced_layer_ranges(cfg, world, rows=rows_total, context=mean_ctx))
         cap = args.prompt + args.warmup + 3 * args.steps + 16
-        for sl in slots:
-            stage.kv_reserve(sl, rows, cap)
-
+        pr = PipelineRank(cfg, groups=n_groups, rows=rows, capacity=cap, layer_ranges=ranges, top_p=top_p)
+        pr.prompt_len = args.prompt
         g = torch.Generator().manual_seed(1000)
-        prompts = [torch.randint(0, cfg.vocab_size, (rows, args.prompt), generator=g).to(dev)
-                   for _ in range(n_groups)]
-        hid_prefill = [torch.empty(rows, args.prompt, H, dtype=torch.bfloat16, device=dev)
-                       for _ in range(n_groups)]
-        hid_decode = [torch.empty(rows, 1, H, dtype=torch.bfloat16, device=dev) for _ in range(n_groups)]
-        ids_bufs = [torch.empty(rows, 1, dtype=torch.int64, device=dev) for _ in range(n_groups)]
-
-        def forward_prefill(k, grp, x):
-            if ring.first:
-                return stage.forward_slot(slots[grp], None, input_ids=x, logits="last", check_values=False)
-            return stage.forward_slot(slots[grp], x, logits="last", check_values=False)
-
-        sample_gen = torch.Generator(device=dev).manual_seed(1234)
-
-        def decode_on(slot_ids, x):
-            # the last stage selects the greedy tokens inside its lm_head
-            if ring.last and top_p is None:
-                return stage.decode_greedy(slot_ids, None if ring.first else x,
-                                           input_ids=x if ring.first else None)[0]
-            if ring.first:
-                return stage.decode_multi(slot_ids, None, input_ids=x, logits="last")
-            return stage.decode_multi(slot_ids, x, logits="last")
-
-        def forward_decode(k, grp, x):
-            return decode_on([slots[grp]], x)
-
-        def tokens_of(out):
-            if out.dtype == torch.int64:  # already selected by decode_greedy
-                return out.view(-1, 1)
-            if top_p is not None:
-                return top_p_sample(out[:, -1], *top_p, generator=sample_gen).unsqueeze(-1)
-            return greedy_sample(out[:, -1]).unsqueeze(-1)
-
-        def sample(k, grp, out):
-            return tokens_of(out).contiguous()
-
-        host_ids = torch.empty(rows, 1, dtype=torch.int64).pin_memory()
-
-        def sample_host(k, grp, out):
-            ids = tokens_of(out)
-            host_ids.copy_(ids, non_blocking=True)  # the server reads every token
-            torch.cuda.current_stream().synchronize()
-            return host_ids.to(dev, non_blocking=True)
-
-        ret_group = dist.new_group(list(range(world)))
-
-        def run(n_steps, inputs, fwd, smp, hid):
-            return decode_loop(ring, n_groups, n_steps, inputs, fwd, smp,
-                               lambda k, grp: hid[grp], lambda grp: ids_bufs[grp],
-                               ret_group=ret_group)
+        prompts_host = [torch.randint(0, cfg.vocab_size, (rows, args.prompt), generator=g)
+                        for _ in range(n_groups)]
+        prompts = [p.to(dev) for p in prompts_host] if ring.first else None
 
         def timed(fn):
             dist.barrier()
@@ -224,70 +352,64 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
 
         # One untimed prefill first (the communicators connect and every kernel
         # is configured on first use), then the caches are rolled back.
-        timed(lambda: run(1, prompts, forward_prefill, sample, hid_prefill))
-        for sl in slots:
-            stage.kv_trim(sl, 0)
-        ids, prefill_ms = timed(lambda: run(1, prompts, forward_prefill, sample, hid_prefill))
-        ids, _ = timed(lambda: run(args.warmup, ids, forward_decode, sample, hid_decode))
+        timed(lambda: pr.prefill(prompts))
+        pr.reset()
+        pr.record = [] if top_p is None else None  # ids of every iteration, for the one-GPU check
+        ids, prefill_ms = timed(lambda: pr.prefill(prompts))
+        ids, _ = timed(lambda: pr.decode(ids, args.warmup))
         launches0 = _launches()
-        from contextlib import nullcontext
-
-        from gpu_mesh_b200.clocks import ClockSampler
-
         with (ClockSampler(local) if ring.first else nullcontext()) as clocks:
-            ids, ms = timed(lambda: run(args.steps, ids, forward_decode, sample, hid_decode))
+            ids, ms = timed(lambda: pr.decode(ids, args.steps))
         launches = _launches() - launches0
-        stage.profile(True)
-        ids, _ = timed(lambda: run(args.steps, ids, forward_decode, sample, hid_decode))
-        prof = stage.profile_read()
-        stage.profile(False)
-        ids, e2e_ms = timed(lambda: run(args.steps, ids, forward_decode, sample_host, hid_decode))
+        pr.stage.profile(True)
+        ids, _ = timed(lambda: pr.decode(ids, args.steps))
+        prof = pr.stage.profile_read()
+        pr.stage.profile(False)
+        ids, e2e_ms = timed(lambda: pr.decode(ids, args.steps, host_tokens=True))
+        record, pr.record = pr.record, None
 
         # Weak scaling: the same per-GPU work at a batch that grows with N
         # (N groups of 32 rows in flight: every GPU streams its weights N
         # times per step, as one GPU streams all weights once for 32 rows).
         weak = None
         if world > 1 and not getattr(args, "no_weak", False):
-            for sl in slots:
-                stage.kv_free(sl)
+            pr.close()
             torch.cuda.empty_cache()
-            rows_w = rows_total
-            slots_w = list(range(101, 101 + n_groups))
-            for sl in slots_w:
-                stage.kv_reserve(sl, rows_w, cap)
+            ranges_w = (split_layers(cfg.num_hidden_layers, world) if getattr(args, "even_split", False) else
+                        balanced_layer_ranges(cfg, world, rows=rows_total * n_groups, context=mean_ctx))
+            pw = PipelineRank(cfg, groups=n_groups, rows=rows_total, capacity=cap, layer_ranges=ranges_w,
+                              top_p=top_p)
+            pw.prompt_len = args.prompt
             gw = torch.Generator().manual_seed(2000)
-            prompts_w = [torch.randint(0, cfg.vocab_size, (rows_w, args.prompt), generator=gw).to(dev)
-                         for _ in range(n_groups)]
-            hid_pw = [torch.empty(rows_w, args.prompt, H, dtype=torch.bfloat16, device=dev)
-                      for _ in range(n_groups)]
-            hid_dw = [torch.empty(rows_w, 1, H, dtype=torch.bfloat16, device=dev) for _ in range(n_groups)]
-            ids_w = [torch.empty(rows_w, 1, dtype=torch.int64, device=dev) for _ in range(n_groups)]
-
-            def fwd_pw(k, grp, x):
-                if ring.first:
-                    return stage.forward_slot(slots_w[grp], None, input_ids=x, logits="last", check_values=False)
-                return stage.forward_slot(slots_w[grp], x, logits="last", check_values=False)
-
-            def fwd_dw(k, grp, x):
-                return decode_on([slots_w[grp]], x)
-
-            def run_w(n_steps, inputs, fwd, hid):
-                return decode_loop(ring, n_groups, n_steps, inputs, fwd, sample,
-                                   lambda k, grp: hid[grp], lambda grp: ids_w[grp], ret_group=ret_group)
-
-            idw, _ = timed(lambda: run_w(1, prompts_w, fwd_pw, hid_pw))
-            idw, _ = timed(lambda: run_w(args.warmup, idw, fwd_dw, hid_dw))
-            idw, ms_w = timed(lambda: run_w(args.steps, idw, fwd_dw, hid_dw))
+            prompts_w = [torch.randint(0, cfg.vocab_size, (rows_total, args.prompt), generator=gw).to(dev)
+                         for _ in range(n_groups)] if ring.first else None
+            idw, _ = timed(lambda: pw.prefill(prompts_w))
+            idw, _ = timed(lambda: pw.decode(idw, args.warmup))
+            idw, ms_w = timed(lambda: pw.decode(idw, args.steps))
+            pw.close()
             weak = {
                 "scaling": "weak",
-                "rows": rows_w * n_groups,
+                "rows": rows_total * n_groups,
                 "groups_in_flight": n_groups,
-                "rows_per_group": rows_w,
-                "value": rows_w * n_groups * args.steps / (ms_w / 1000.0),
+                "rows_per_group": rows_total,
+                "layer_ranges": ranges_w,
+                "value": rows_total * n_groups * args.steps / (ms_w / 1000.0),
                 "unit": "tok/s",
                 "ms_per_step": ms_w / args.steps,
                 "note": "per-GPU work of the one-GPU workload (32 rows through every layer once per step)",
             }
+        else:
+            pr.close()
+        torch.cuda.empty_cache()
+
+        # Token check: the last stage replays the run with the whole model on
+        # its own GPU (the one-GPU path), teacher-forced on the pipeline's ids.
+        check = None
+        if ring.last and record is not None:
+            check = verify_one_gpu(cfg, prompts_host, record, n_groups, device=dev)
+        checks = [None] * world
+        dist.all_gather_object(checks, check)
+        check = checks[-1]
 
         profs = [None] * world
         dist.all_gather_object(profs, prof)
@@ -300,6 +422,7 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
             att_b, att_ms = sum(p["bytes"] for p in att), sum(p["ms"] for p in att)
             lin_gbs = lin_b / (lin_ms / 1000) / 1e9 if lin_ms else 0.0
             att_gbs = att_b / (att_ms / 1000) / 1e9 if att_ms else 0.0
+            stage_ms = [sum(c["ms"] for c in p.values()) / args.steps for p in profs]
             line = {
                 "metric": metric,
                 "value": rows_total * args.steps / (ms / 1000.0),
@@ -314,7 +437,7 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 "dtype": "bf16",
                 "data": "synthetic (random-init N(0,0.02) weights, uniform-random prompt ids)",
                 "config": {**workload, "stages": world, "parallelism": f"pp{world}",
-                           "groups_in_flight": n_groups, "rows_per_group": rows},
+                           "groups_in_flight": n_groups, "rows_per_group": rows, "layer_ranges": ranges},
                 # Bytes and kernel time are summed over the stages, each on its
                 # own GPU, so the ratios are per-GPU rates.
                 "roofline": {
@@ -330,7 +453,7 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 },
                 "attention_roofline": {
                     "bound": "hbm",
-                    "kernel": "attn_tc + attn_combine, mean over stages",
+                    "kernel": "attn_tc, mean over stages",
                     "achieved": att_gbs,
                     "peak": hbm,
                     "unit": "GB/s",
@@ -346,13 +469,15 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 },
                 "prefill": {"tok_s": rows_total * args.prompt / (prefill_ms / 1000.0), "ms": prefill_ms},
                 "gpu_launches": int(sum(counts)),
+                "per_stage_ms_per_step": stage_ms,
                 "per_stage_profile": profs,
                 "clocks": clocks.summary(),
             }
+            if check is not None:
+                line["token_check"] = check
             if weak is not None:
                 line["weak_scaling"] = weak
             print(json.dumps(line), flush=True)
-        stage.close()
     finally:
         dist.barrier()
         dist.destroy_process_group()

@@ -44,6 +44,40 @@ class _LoadResult(NamedTuple):
     unexpected_keys: list[str]
 
 
+class _Submodule:
+    """A named part of the stage (``embed_tokens``, ``norm``, ``lm_head``,
+    ``layers[i]``) with the nn.Module weight methods callers use on the
+    reference's LlamaStage submodules, over the stage's own HBM views."""
+
+    def __init__(self, stage: "B200Stage", prefix: str) -> None:
+        self._stage, self._prefix = stage, prefix + "."
+
+    def named_parameters(self):
+        n = len(self._prefix)
+        for k, v in self._stage.named_parameters():
+            if k.startswith(self._prefix):
+                yield k[n:], v
+
+    def parameters(self):
+        for _, v in self.named_parameters():
+            yield v
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        n = len(self._prefix)
+        return {k[n:]: v for k, v in self._stage.state_dict().items() if k.startswith(self._prefix)}
+
+    def load_state_dict(self, state_dict: dict[str, torch.Tensor], strict: bool = True):
+        own = self.state_dict()
+        missing = [k for k in own if k not in state_dict]
+        unexpected = [k for k in state_dict if k not in own]
+        if strict and (missing or unexpected):
+            raise RuntimeError(f"Error(s) in loading state_dict for {self._prefix[:-1]}: missing keys "
+                               f"{missing}, unexpected keys {unexpected}")
+        full = {self._prefix + k: v for k, v in state_dict.items() if k in own}
+        self._stage.load_state_dict(full, strict=False)
+        return _LoadResult(missing, unexpected)
+
+
 class B200Stage:
     """Contiguous decoder layers [layer_start, layer_end) on one B200.
 
@@ -437,6 +471,14 @@ class B200Stage:
         _lib.check(self._lib.mg_stage_profile_read(self.handle, ctypes.byref(prof)))
         return prof.as_dict()
 
+    def probe_wait(self, limit_us: int, *, flag_set: bool = False) -> None:
+        """Queue a bounded wait for the stage's probe flag (set only with
+        ``flag_set``); unset, it runs out after ``limit_us`` and records the
+        timeout code, which the next ``check_device`` raises as
+        ``DeviceTimeoutError``."""
+        _lib.check(self._lib.mg_stage_probe_wait(self.handle, int(limit_us), int(flag_set),
+                                                 _stream(self.device)))
+
     def check_device(self) -> None:
         """Raise if a kernel clamped an out-of-range id or position since the last check."""
         _lib.check(self._lib.mg_stage_check_device(self.handle, _stream(self.device)))
@@ -491,6 +533,30 @@ class B200Stage:
     def parameters(self):
         for _, t in self.named_parameters():
             yield t
+
+    # The reference stage's submodules, as weight views (absent where the
+    # reference's would be: no embedding off the first stage, no head off the last).
+    @property
+    def embed_tokens(self) -> _Submodule:
+        if not self.has_embedding:
+            raise AttributeError("this stage has no embed_tokens")
+        return _Submodule(self, "embed_tokens")
+
+    @property
+    def norm(self) -> _Submodule:
+        if not self.has_lm_head:
+            raise AttributeError("this stage has no norm")
+        return _Submodule(self, "norm")
+
+    @property
+    def lm_head(self) -> _Submodule:
+        if not self.has_lm_head:
+            raise AttributeError("this stage has no lm_head")
+        return _Submodule(self, "lm_head")
+
+    @property
+    def layers(self) -> list[_Submodule]:
+        return [_Submodule(self, f"layers.{i}") for i in range(self.layer_end - self.layer_start)]
 
     def state_dict(self) -> dict[str, torch.Tensor]:
         """Every weight under its reference name (a tied head under both names)."""

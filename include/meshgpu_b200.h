@@ -34,6 +34,7 @@ extern "C" {
 #define MG_ECUDA 3
 #define MG_ENOMEM 4
 #define MG_EDEVICE 5 /* a kernel recorded an out-of-range id or position */
+#define MG_ETIMEOUT 6 /* a kernel gave up a bounded wait (about 2 s); its outputs are invalid */
 
 #define MG_DTYPE_F32 0
 #define MG_DTYPE_BF16 1
@@ -234,6 +235,17 @@ int mg_stage_decode_greedy(mg_stage* stage, const int32_t* slots, int32_t n_slot
  * Returns MG_EDEVICE with a message when a kernel met an out-of-range token
  * id or position since the last check. */
 int mg_stage_check_device(mg_stage* stage, void* stream);
+
+/* Exercise the stage's timeout path without a fault: one thread waits, with
+ * the same bounded wait every kernel of the stage uses, for a flag word of the
+ * stage that is set only when `flag_set` is non-zero.  With the flag unset the
+ * wait runs out after `limit_us` (1 .. 2e6) and records code 3 in the stage's
+ * error word, exactly as a starved tensor-core kernel would; the next
+ * mg_stage_check_device returns MG_ETIMEOUT and resets the stage's counters.
+ * Nothing else is in flight during the wait.  Instrumentation; no
+ * counterpart in the reference, which tests failures on the host only
+ * (tests/unit/test_inference.py:196-233). */
+int mg_stage_probe_wait(mg_stage* stage, uint32_t limit_us, int32_t flag_set, void* stream);
 
 /* ---- Single linear layer (the stage's GEMM paths: weight-streaming GEMV
  * for <= 32 rows, tcgen05 GEMM above, SIMT for fp32) ---- */

@@ -166,3 +166,63 @@ def test_cancelled_stream_releases_its_context():
     w, first, b = asyncio.run(main())
     assert first.token_id == next_token(3)
     assert b.active_count == 0 and w.caches == {}
+
+
+def test_a_failing_request_does_not_end_the_others():
+    import threading
+
+    class Flaky(FakeWorker):
+        def __init__(self):
+            super().__init__()
+            self.bad = None
+            self.armed = threading.Event()
+
+        def decode_multi(self, hidden, cache_keys, **kw):
+            self.armed.wait(5)  # the test names the failing context before any decode
+            if self.bad in cache_keys:
+                raise RuntimeError("stage failure")
+            return super().decode_multi(hidden, cache_keys, **kw)
+
+        def forward_inference(self, hidden, **kw):
+            if self.bad is not None and kw.get("cache_key") == self.bad:
+                raise RuntimeError("stage failure")
+            return super().forward_inference(hidden, **kw)
+
+    async def main():
+        w = Flaky()
+        b = B.ContinuousBatcher([w], max_batch_size=4)
+        b.start()
+        bad = await b.submit([1], SamplingParams(), 6)
+        good = await b.submit([2], SamplingParams(), 6)
+        w.bad = f"seq:{bad}"
+        w.armed.set()
+        res_bad, res_good = await asyncio.gather(_collect(b, bad), _collect(b, good))
+        b.stop()
+        await b.wait_stopped()
+        return w, res_bad, res_good
+
+    w, res_bad, res_good = asyncio.run(main())
+    assert [r.token_id for r in res_good] == expected([2], 6)
+    assert res_bad[-1].token_id == -1 and res_bad[-1].is_last  # at its prefill or its first decode
+    assert w.caches == {}
+
+
+def test_stop_ends_running_requests_and_releases_them():
+    async def main():
+        w = FakeWorker()
+        b = B.ContinuousBatcher([w], max_batch_size=2)
+        b.start()
+        sid = await b.submit([5], SamplingParams(), 60)
+        agen = b.stream(sid)
+        first = await agen.__anext__()
+        b.stop()
+        rest = [r async for r in agen]
+        await b.wait_stopped()
+        with pytest.raises(RuntimeError, match="not running"):
+            await b.submit([1], SamplingParams(), 1)
+        return w, first, rest
+
+    w, first, rest = asyncio.run(main())
+    assert first.seq_num == 1
+    assert rest[-1].token_id == -1 and rest[-1].is_last
+    assert w.caches == {}

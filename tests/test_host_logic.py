@@ -311,3 +311,20 @@ def test_boundary_transports_on_the_host():
     assert move_to_stage(x, "cpu", transport="local_cuda") is x
     with pytest.raises(ValueError, match="unsupported local boundary transport"):
         move_to_stage(x, "cpu", transport="rdma")
+
+
+def test_balanced_layer_ranges_even_out_the_streamed_bytes():
+    from gpu_mesh_b200.config import balanced_layer_ranges
+
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192)
+    for n in (1, 2, 4, 8):
+        r = balanced_layer_ranges(cfg, n, rows=32, context=1100)
+        assert r[0][0] == 0 and r[-1][1] == 32 and all(a[1] == b[0] and a[0] < a[1] for a, b in zip(r, r[1:]))
+    r8 = balanced_layer_ranges(cfg, 8, rows=32, context=1100)
+    sizes = [b - a for a, b in r8]
+    assert sizes[-1] < min(sizes[:-1])  # the lm_head stage holds fewer layers
+    assert max(sizes) == 5  # 32 layers + lm_head cannot spread thinner than 5 layers on some stage
+    assert balanced_layer_ranges(cfg, 1, rows=1, context=1) == [(0, 32)]
+    with pytest.raises(ValueError):
+        balanced_layer_ranges(cfg, 33, rows=1, context=1)
