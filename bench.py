@@ -92,6 +92,28 @@ def model_config(name: str, layers: int | None = None):
                        mask_policy="cache")
 
 
+def other_configs(world: int) -> list[dict]:
+    """The scope's configurations that name this stage count, measured beside
+    the headline line of an N-GPU run: TinyLlama-1.1B on 2 stages; Qwen3-4B
+    (top-p) on 2 and 4; the long-context Llama-3-8B stress (64 rows, caches
+    pre-filled to 8192 positions) on 8."""
+    out = []
+    if world == 2:
+        out.append({"name": "tinyllama-1.1b", "cfg": model_config("tinyllama-1.1b"), "rows": 8, "prompt": 512,
+                    "note": "TinyLlama-1.1B arch, bf16, batch 8, 512-token prompts, greedy"})
+    if world in (2, 4):
+        out.append({"name": "qwen3-4b", "cfg": model_config("qwen3-4b"), "rows": 16, "prompt": 2048,
+                    "top_p": TOP_P, "note": "Qwen3-4B arch, bf16, batch 16, 2048-token prompts, top-p "
+                                            "(T 0.7, p 0.9, seeded)"})
+    if world == 8:
+        cfg = llama3_8b(32)
+        cfg.max_position_embeddings = 8192 + 256
+        out.append({"name": "llama3-8b-long-context", "cfg": cfg, "rows": 64, "context": 8192,
+                    "note": "Llama-3-8B arch, bf16, batch 64, every stage's caches pre-filled to 8192 "
+                            "positions with N(0,1), greedy"})
+    return out
+
+
 def metric_for(args) -> str:
     if args.model == "llama3-8b":
         return METRIC
@@ -518,6 +540,10 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-weak", action="store_true",
                     help="N > 1: skip the weak-scaling measurement (N groups of 32 rows in flight)")
+    ap.add_argument("--nccl-sms", type=int, default=8,
+                    help="N > 1: SMs each GPU leaves out of its persistent kernels for NCCL's kernels")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="N > 1: skip the other configurations named at this stage count")
     ap.add_argument("--even-split", action="store_true",
                     help="N > 1: the reference's even layer split instead of ranges that even out the "
                          "bytes each stage streams")
@@ -537,9 +563,12 @@ def main() -> None:
         return
     from gpu_mesh_b200.dist import run_pipeline_bench
 
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     run_pipeline_bench(args, model_config(args.model, args.layers), metric_for(args), workload_config(args), peaks(),
                        NCU_TRAFFIC if args.model == "llama3-8b" else None,
-                       top_p=None if MODELS[args.model]["sampling"] == "greedy" else TOP_P)
+                       top_p=None if MODELS[args.model]["sampling"] == "greedy" else TOP_P,
+                       other_configs=[] if args.no_other_configs or args.model != "llama3-8b"
+                       else other_configs(world))
 
 
 if __name__ == "__main__":

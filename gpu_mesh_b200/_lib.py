@@ -203,6 +203,7 @@ SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i3
 SIGNATURES["mg_linear_check_device"] = (ctypes.c_int, [_vp])
 SIGNATURES["mg_stage_probe_wait"] = (ctypes.c_int, [_vp, ctypes.c_uint32, _i32, _vp])
 SIGNATURES["mg_stage_weight"] = (ctypes.c_int, [_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)])
+SIGNATURES["mg_reserve_sms"] = (ctypes.c_int, [_i32, _i32])
 SIGNATURES["mg_peer_access"] = (ctypes.c_int, [_i32, _i32, ctypes.POINTER(ctypes.c_int32)])
 SIGNATURES["mg_peer_copy"] = (ctypes.c_int, [_vp, _i32, _vp, _i32, ctypes.c_uint64, _vp])
 SIGNATURES["mg_linear_noalloc"] = (

@@ -54,6 +54,30 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
 
+}  // namespace
+
+namespace mg {
+
+std::atomic<int> g_reserved_sms[64];
+
+int usable_sms() {
+  static int full[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!full[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    full[dev] = v > 0 ? v : 148;
+  }
+  const int n = full[dev] - g_reserved_sms[dev].load();
+  return n > 1 ? n : 1;
+}
+
+}  // namespace mg
+
+namespace {
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -1269,6 +1293,15 @@ int mg_linear_check_device(void* stream) {
   return fail(MG_ETIMEOUT, "a linear launch gave up waiting for its data (code %d); its output is invalid", h);
 }
 
+int mg_reserve_sms(int32_t device, int32_t n) {
+  int count = 0;
+  if (device < 0 || device >= 64) return fail(MG_EINVAL, "device ordinal %d out of range", device);
+  MG_CUDA(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device), "SM count");
+  if (n < 0 || n > count / 2) return fail(MG_EINVAL, "reserve between 0 and %d SMs", count / 2);
+  mg::g_reserved_sms[device].store(n);
+  return MG_OK;
+}
+
 int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled) {
   if (!enabled) return fail(MG_EINVAL, "null argument");
   *enabled = 0;
@@ -1294,6 +1327,7 @@ int mg_peer_copy(void* dst, int32_t dst_device, const void* src, int32_t src_dev
                  void* stream) {
   if ((!dst || !src) && bytes) return fail(MG_EINVAL, "null buffer");
   if (bytes == 0) return MG_OK;
+  DeviceGuard guard(src_device);  // the stream belongs to the source device
   MG_CUDA(cudaMemcpyPeerAsync(dst, dst_device, src, src_device, (size_t)bytes, (cudaStream_t)stream),
           "cudaMemcpyPeerAsync");
   return MG_OK;

@@ -117,4 +117,9 @@ __device__ __forceinline__ void flag_error(int* err, int code) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Streaming multiprocessors a persistent kernel spreads over on the current
+// device: the device's count minus the SMs left free for concurrent work
+// (NCCL's kernels in a multi-process pipeline; mg_reserve_sms).  Host code.
+int usable_sms();
+
 }  // namespace mg

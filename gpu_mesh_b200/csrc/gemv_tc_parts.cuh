@@ -39,18 +39,9 @@ struct Part {
   __host__ __device__ int slot(int c, int t) const { return 2 * c + (t == begin(c) / nk ? 0 : 1); }
 };
 
-// Streaming multiprocessors of the current device (cached per device).
+// Persistent grid size on the current device (usable_sms).
 inline int sm_count() {
-  static int n[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!n[dev]) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    n[dev] = v > 0 ? v : 148;
-  }
-  return n[dev];
+  return usable_sms();
 }
 
 // Tiles of 128 W rows (64 gate + 64 up rows for SwiGLU) x K/64 blocks, cut

@@ -490,16 +490,7 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
 }
 
 int sm_count_attn() {
-  static int n[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!n[dev]) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    n[dev] = v > 0 ? v : 148;
-  }
-  return n[dev];
+  return usable_sms();
 }
 
 }  // namespace

@@ -140,7 +140,9 @@ class PipelineRank:
 
     def __init__(self, cfg, *, groups: int, rows: int, capacity: int, layer_ranges=None,
                  dtype: torch.dtype = torch.bfloat16, seed: int = 0, method: str = "portable",
-                 state_dict=None, top_p: tuple[float, float] | None = None, sample_seed: int = 1234) -> None:
+                 state_dict=None, top_p: tuple[float, float] | None = None, sample_seed: int = 1234,
+                 nccl_sms: int = 8) -> None:
+        from gpu_mesh_b200 import _lib
         from gpu_mesh_b200.config import split_layers
         from gpu_mesh_b200.stage import B200Stage
         from gpu_mesh_b200.weights import synthetic_stage_state
@@ -148,6 +150,10 @@ class PipelineRank:
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
         self.ring = Ring(self.rank, self.world)
         self.device = torch.device("cuda", torch.cuda.current_device())
+        # NCCL's send/receive kernels run beside the stage's persistent kernels
+        # for most of a step: leave them SMs of their own, so no CTA of a
+        # stream-K GEMM or of the attention waits for one.
+        _lib.check(_lib.lib().mg_reserve_sms(self.device.index, nccl_sms if self.world > 1 else 0))
         self.cfg = cfg
         self.ranges = list(layer_ranges or split_layers(cfg.num_hidden_layers, self.world))
         ls, le = self.ranges[self.rank]
@@ -236,6 +242,19 @@ class PipelineRank:
         for sl in self.slots:
             self.stage.kv_trim(sl, 0)
 
+    def import_random_kv(self, context: int, seed: int = 5) -> None:
+        """Fill every group's cache on this stage to ``context`` positions with
+        N(0, 1) keys and values (a long-context decode without a prefill)."""
+        cfg = self.cfg
+        g = torch.Generator(device=self.device).manual_seed(seed + self.rank)
+        shape = (self.rows, cfg.num_key_value_heads, context, cfg.head_dim)
+        for sl in self.slots:
+            for layer in range(self.stage.layer_end - self.stage.layer_start):
+                k = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
+                v = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
+                self.stage.kv_import(sl, layer, k, v)
+                del k, v
+
     def close(self) -> None:
         self.stage.close()
 
@@ -304,9 +323,12 @@ def verify_one_gpu(cfg, prompts: list[torch.Tensor], record: list[tuple[int, tor
 # ---------------------------------------------------------------------------
 
 def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[float, float, str],
-                       traffic: dict | None = None, top_p: tuple[float, float] | None = None) -> None:
+                       traffic: dict | None = None, top_p: tuple[float, float] | None = None,
+                       other_configs: list[dict] | None = None) -> None:
     """``top_p`` = (temperature, p): the last stage samples with a seeded device
-    generator instead of selecting greedily inside its lm_head."""
+    generator instead of selecting greedily inside its lm_head.
+    ``other_configs``: the scope's configurations named at this stage count,
+    measured after the headline one (``run_other_config``)."""
     from contextlib import nullcontext
 
     from gpu_mesh_b200.clocks import ClockSampler
@@ -330,7 +352,9 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
         ranges = (split_layers(cfg.num_hidden_layers, world) if getattr(args, "even_split", False) else
                   balanced_layer_ranges(cfg, world, rows=rows_total, context=mean_ctx))
         cap = args.prompt + args.warmup + 3 * args.steps + 16
-        pr = PipelineRank(cfg, groups=n_groups, rows=rows, capacity=cap, layer_ranges=ranges, top_p=top_p)
+        nccl_sms = getattr(args, "nccl_sms", 8)
+        pr = PipelineRank(cfg, groups=n_groups, rows=rows, capacity=cap, layer_ranges=ranges, top_p=top_p,
+                          nccl_sms=nccl_sms)
         pr.prompt_len = args.prompt
         g = torch.Generator().manual_seed(1000)
         prompts_host = [torch.randint(0, cfg.vocab_size, (rows, args.prompt), generator=g)
@@ -378,7 +402,7 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
             ranges_w = (split_layers(cfg.num_hidden_layers, world) if getattr(args, "even_split", False) else
                         balanced_layer_ranges(cfg, world, rows=rows_total * n_groups, context=mean_ctx))
             pw = PipelineRank(cfg, groups=n_groups, rows=rows_total, capacity=cap, layer_ranges=ranges_w,
-                              top_p=top_p)
+                              top_p=top_p, nccl_sms=nccl_sms)
             pw.prompt_len = args.prompt
             gw = torch.Generator().manual_seed(2000)
             prompts_w = [torch.randint(0, cfg.vocab_size, (rows_total, args.prompt), generator=gw).to(dev)
@@ -411,6 +435,10 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
         dist.all_gather_object(checks, check)
         check = checks[-1]
 
+        others = {}
+        for spec in other_configs or []:
+            others[spec["name"]] = run_other_config(spec, args, timed)
+
         profs = [None] * world
         dist.all_gather_object(profs, prof)
         counts = [0] * world
@@ -437,7 +465,8 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                 "dtype": "bf16",
                 "data": "synthetic (random-init N(0,0.02) weights, uniform-random prompt ids)",
                 "config": {**workload, "stages": world, "parallelism": f"pp{world}",
-                           "groups_in_flight": n_groups, "rows_per_group": rows, "layer_ranges": ranges},
+                           "groups_in_flight": n_groups, "rows_per_group": rows, "layer_ranges": ranges,
+                           "sms_left_to_nccl": nccl_sms},
                 # Bytes and kernel time are summed over the stages, each on its
                 # own GPU, so the ratios are per-GPU rates.
                 "roofline": {
@@ -475,12 +504,59 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
             }
             if check is not None:
                 line["token_check"] = check
+            if others:
+                line["other_configs"] = others
             if weak is not None:
                 line["weak_scaling"] = weak
             print(json.dumps(line), flush=True)
     finally:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_other_config(spec: dict, args, timed) -> dict:
+    """One of the scope's other configurations on this pipeline (every rank
+    calls it): ``spec`` = {name, cfg, rows, prompt | context, top_p, note}.
+    Greedy (or seeded top-p) decode with the N ranks' groups in flight; a
+    ``context`` spec starts from caches pre-filled with N(0, 1) instead of a
+    prefill.  Returns tok/s, ms per step and the prefill rate."""
+    from gpu_mesh_b200.config import balanced_layer_ranges
+
+    world = dist.get_world_size()
+    cfg, rows_total = spec["cfg"], spec["rows"]
+    groups = world
+    if rows_total % groups:
+        raise ValueError(f"{rows_total} rows do not split into {groups} groups")
+    rows = rows_total // groups
+    start = spec.get("context") or spec["prompt"]
+    cap = start + args.warmup + args.steps + 8
+    ranges = balanced_layer_ranges(cfg, world, rows=rows_total, context=start)
+    pr = PipelineRank(cfg, groups=groups, rows=rows, capacity=cap, layer_ranges=ranges, top_p=spec.get("top_p"),
+                      nccl_sms=getattr(args, "nccl_sms", 8))
+    try:
+        dev = pr.device
+        out = {"config": spec["note"], "stages": world, "rows": rows_total, "groups_in_flight": groups,
+               "layer_ranges": ranges}
+        g = torch.Generator().manual_seed(3000)
+        if spec.get("context"):
+            pr.import_random_kv(spec["context"])
+            ids = ([torch.randint(0, cfg.vocab_size, (rows, 1), generator=g).to(dev) for _ in range(groups)]
+                   if pr.ring.first else None)
+        else:
+            pr.prompt_len = spec["prompt"]
+            prompts = ([torch.randint(0, cfg.vocab_size, (rows, spec["prompt"]), generator=g).to(dev)
+                        for _ in range(groups)] if pr.ring.first else None)
+            ids, pf_ms = timed(lambda: pr.prefill(prompts))
+            out["prefill_tok_s"] = rows_total * spec["prompt"] / (pf_ms / 1000.0)
+        ids, _ = timed(lambda: pr.decode(ids, args.warmup))
+        ids, ms = timed(lambda: pr.decode(ids, args.steps))
+        out.update({"decode_tok_s": rows_total * args.steps / (ms / 1000.0), "ms_per_step": ms / args.steps,
+                    "steps": args.steps})
+        pr.stage.check_device()
+        return out
+    finally:
+        pr.close()
+        torch.cuda.empty_cache()
 
 
 def _launches() -> int:

@@ -33,10 +33,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
     n_scr = lib.mg_linear_scratch(_DT[x.dtype], M, N, K, code)
     scratch = torch.empty(max(int(n_scr), 1), dtype=torch.float32, device=x.device)
     r = residual if residual is not None else None
-    _lib.check(lib.mg_linear(
-        _DT[x.dtype], x.data_ptr(), x.stride(0), w.data_ptr(), M, N, K, code,
-        None if r is None else r.data_ptr(), 0 if r is None else r.stride(0),
-        out.data_ptr(), out.stride(0), scratch.data_ptr(), scratch.numel(),
-        torch.cuda.current_stream(x.device).cuda_stream,
-    ))
+    with torch.cuda.device(x.device):  # the kernel runs on x's GPU, on its current stream
+        _lib.check(lib.mg_linear(
+            _DT[x.dtype], x.data_ptr(), x.stride(0), w.data_ptr(), M, N, K, code,
+            None if r is None else r.data_ptr(), 0 if r is None else r.stride(0),
+            out.data_ptr(), out.stride(0), scratch.data_ptr(), scratch.numel(),
+            torch.cuda.current_stream(x.device).cuda_stream,
+        ))
     return out

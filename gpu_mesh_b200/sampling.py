@@ -77,12 +77,13 @@ def greedy_sample(logits: torch.Tensor) -> torch.Tensor:
     """Argmax over the last dimension, lowest index on ties (sampling.py:58-60)."""
     flat, lead = _rows(logits)
     ids = torch.empty(flat.shape[0], dtype=torch.int64, device=flat.device)
-    _lib.check(
-        _lib.lib().mg_sample_greedy(
-            flat.data_ptr(), _DT[flat.dtype], flat.shape[0], flat.shape[1], flat.stride(0),
-            ids.data_ptr(), torch.cuda.current_stream(flat.device).cuda_stream,
+    with torch.cuda.device(flat.device):  # the kernel runs on the logits' GPU, on its current stream
+        _lib.check(
+            _lib.lib().mg_sample_greedy(
+                flat.data_ptr(), _DT[flat.dtype], flat.shape[0], flat.shape[1], flat.stride(0),
+                ids.data_ptr(), torch.cuda.current_stream(flat.device).cuda_stream,
+            )
         )
-    )
     return ids.reshape(lead)
 
 
@@ -108,11 +109,12 @@ def top_p_sample(
         uniforms = torch.rand(rows, generator=generator, device=gen_device)
     uniforms = uniforms.to(device=flat.device, dtype=torch.float32).reshape(rows).contiguous()
     ids = torch.empty(rows, dtype=torch.int64, device=flat.device)
-    _lib.check(
-        _lib.lib().mg_sample_top_p(
-            flat.data_ptr(), _DT[flat.dtype], rows, flat.shape[1], flat.stride(0),
-            float(temperature), float(top_p), uniforms.data_ptr(), ids.data_ptr(),
-            torch.cuda.current_stream(flat.device).cuda_stream,
+    with torch.cuda.device(flat.device):
+        _lib.check(
+            _lib.lib().mg_sample_top_p(
+                flat.data_ptr(), _DT[flat.dtype], rows, flat.shape[1], flat.stride(0),
+                float(temperature), float(top_p), uniforms.data_ptr(), ids.data_ptr(),
+                torch.cuda.current_stream(flat.device).cuda_stream,
+            )
         )
-    )
     return ids.reshape(lead)

@@ -154,7 +154,8 @@ class B200Stage:
             lw.gate_proj = hold(get(p + "mlp.gate_proj.weight"))
             lw.up_proj = hold(get(p + "mlp.up_proj.weight"))
             lw.down_proj = hold(get(p + "mlp.down_proj.weight"))
-        cos, sin = rope_tables(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta, dtype)
+        cos, sin = rope_tables(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta, dtype,
+                               round_inv_freq=cfg.mask_policy == "cache")
         weights = _lib.StageWeights()
         weights.rope_cos = hold(cos.to(device))
         weights.rope_sin = hold(sin.to(device))

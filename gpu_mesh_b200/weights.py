@@ -287,15 +287,22 @@ def slice_stage_state(
 
 
 def rope_tables(
-    head_dim: int, max_positions: int, theta: float, dtype: torch.dtype
+    head_dim: int, max_positions: int, theta: float, dtype: torch.dtype, *, round_inv_freq: bool = False
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin [max_positions, head_dim/2] on the host, cast to the activation dtype.
 
     Formula of _precompute_freqs (models/llama_dense.py:96-104), which HF's
     default Qwen3 rotary embedding shares; the cast matches
     ``self.rope_cos.to(x.dtype)`` (llama_dense.py:431-432).
+    ``round_inv_freq``: the HF Qwen3 stage keeps the inverse frequencies as a
+    module buffer, and Qwen3Stage casts the whole module to the stage dtype
+    (models/qwen3_hf.py:139-140), so a bf16 Qwen3 stage rotates with
+    frequencies rounded to bf16 (the angles are then formed in fp32,
+    Qwen3RotaryEmbedding.forward).
     """
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))
+    if round_inv_freq:
+        inv = inv.to(dtype).float()
     t = torch.arange(max_positions).float()
     freqs = torch.outer(t, inv)
     return freqs.cos().to(dtype), freqs.sin().to(dtype)

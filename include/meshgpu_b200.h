@@ -337,9 +337,16 @@ uint64_t mg_launch_count(void);
  * 0 if copies between them must stage through host memory. */
 int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled);
 
+/* Leave `n` SMs of `device` (0 <= n <= half of them) out of the persistent
+ * decode kernels' grids (the decode GEMM, decode and prefill attention, the
+ * layer chain), so kernels that run beside them (NCCL's send/receive
+ * kernels in a multi-process pipeline) never hold back one of their CTAs.
+ * Set it before the stage runs; 0 by default. */
+int mg_reserve_sms(int32_t device, int32_t n);
+
 /* Queue a copy of `bytes` from `src` on `src_device` to `dst` on `dst_device`
- * on `stream` (cudaMemcpyPeerAsync: direct over NVLink when peer access is
- * enabled). */
+ * on `stream`, a stream of `src_device` (cudaMemcpyPeerAsync, issued with
+ * `src_device` current: direct over NVLink when peer access is enabled). */
 int mg_peer_copy(void* dst, int32_t dst_device, const void* src, int32_t src_device, uint64_t bytes,
                  void* stream);
 

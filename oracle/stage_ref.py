@@ -28,9 +28,16 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def rope_tables(cfg, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
-    """_precompute_freqs (llama_dense.py:96-104) cast as at :431-432."""
+    """_precompute_freqs (llama_dense.py:96-104) cast as at :431-432.
+
+    HF Qwen3 stages (mask_policy "cache") hold the inverse frequencies as a
+    buffer that Qwen3Stage's ``self.to(dtype)`` rounds to the stage dtype
+    (qwen3_hf.py:139-140); Qwen3RotaryEmbedding.forward then forms the angles
+    from them in fp32 and casts cos/sin to the activation dtype."""
     dim = cfg.head_dim
     freqs = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2).float() / dim))
+    if getattr(cfg, "mask_policy", "llama") == "cache":
+        freqs = freqs.to(dtype).float()
     t = torch.arange(cfg.max_position_embeddings).float()
     f = torch.outer(t, freqs)
     return f.cos().to(dtype), f.sin().to(dtype)

@@ -101,6 +101,16 @@ def test_rope_tables_match_hf_qwen3_rotary_embedding():
     cos_hf, sin_hf = emb(torch.zeros(1, dtype=torch.bfloat16), pos)
     cos, sin = rope_tables(128, 64, 1e6, torch.bfloat16)
     assert torch.equal(cos_hf[0, :, :64], cos) and torch.equal(sin_hf[0, :, :64], sin)
+    # A bf16 Qwen3Stage casts the rotary module to bf16 (qwen3_hf.py:139-140),
+    # rounding its inverse frequencies; at long positions that moves the angles.
+    emb.to(torch.bfloat16)
+    pos = torch.arange(4096).unsqueeze(0)
+    hf.max_position_embeddings = 4096
+    cos_hf, sin_hf = emb(torch.zeros(1, dtype=torch.bfloat16), pos)
+    cos, sin = rope_tables(128, 4096, 1e6, torch.bfloat16, round_inv_freq=True)
+    assert torch.equal(cos_hf[0, :, :64], cos) and torch.equal(sin_hf[0, :, :64], sin)
+    plain, _ = rope_tables(128, 4096, 1e6, torch.bfloat16)
+    assert not torch.equal(plain, cos)
 
 
 def test_sampling_params_validation():
