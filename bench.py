@@ -339,9 +339,7 @@ def long_context(hbm: float, *, rows: int = 64, context: int = 8192, layers: int
 
 def run_single(args) -> None:
     from gpu_mesh_b200 import _lib, build_pipeline, greedy_sample
-    from gpu_mesh_b200.pipeline import pipeline_decode_greedy, pipeline_decode_multi
-
-    from gpu_mesh_b200.sampling import top_p_sample
+    from gpu_mesh_b200.pipeline import pipeline_decode_greedy, pipeline_decode_top_p
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -375,12 +373,15 @@ def run_single(args) -> None:
     stage.check_device()  # a kernel that gave up waiting would make every number below meaningless
     ids = torch.cat(first).unsqueeze(-1)
 
+    rows_all = args.micro * args.micro_batches
+
     def step(ids):
         if greedy:
             tokens, _ = w.decode_greedy(None, keys, input_ids=ids)  # selection fused into lm_head
-        else:
-            logits = w.decode_multi(None, keys, input_ids=ids, logits="last")
-            tokens = top_p_sample(logits[:, -1], *TOP_P, generator=sample_gen)
+        else:  # top-p drawn from the value histograms counted in lm_head's epilogue
+            u = torch.rand(rows_all, generator=sample_gen, device=dev)
+            tokens, _ = w.decode_top_p(None, keys, input_ids=ids, temperature=TOP_P[0], top_p=TOP_P[1],
+                                       uniforms=u)
         return tokens.unsqueeze(-1)
 
     for _ in range(args.warmup):
@@ -420,8 +421,8 @@ def run_single(args) -> None:
         if greedy:
             tok, _ = pipeline_decode_greedy(workers, d_ids, cache_keys=keys)
         else:
-            logits = pipeline_decode_multi(workers, d_ids, cache_keys=keys)
-            tok = top_p_sample(logits[:, -1], *TOP_P, generator=sample_gen)
+            tok, _ = pipeline_decode_top_p(workers, d_ids, cache_keys=keys, temperature=TOP_P[0],
+                                           top_p=TOP_P[1], generator=sample_gen)
         tok = tok.unsqueeze(-1)
         host_out.copy_(tok, non_blocking=True)
         torch.cuda.current_stream().synchronize()

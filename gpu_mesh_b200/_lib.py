@@ -201,6 +201,8 @@ SIGNATURES["mg_linear"] = (
 )
 SIGNATURES["mg_linear_scratch"] = (ctypes.c_uint64, [_i32, _i32, _i32, _i32, _i32])
 SIGNATURES["mg_linear_check_device"] = (ctypes.c_int, [_vp])
+SIGNATURES["mg_stage_decode_top_p"] = (
+    ctypes.c_int, [_vp, _i32p, _i32, _vp, _vp, ctypes.c_float, ctypes.c_float, _vp, _vp, _vp, _vp])
 SIGNATURES["mg_stage_probe_wait"] = (ctypes.c_int, [_vp, ctypes.c_uint32, _i32, _vp])
 SIGNATURES["mg_stage_weight"] = (ctypes.c_int, [_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)])
 SIGNATURES["mg_reserve_sms"] = (ctypes.c_int, [_i32, _i32])

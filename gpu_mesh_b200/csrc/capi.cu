@@ -461,9 +461,15 @@ int linear_class(const LinearArgs& a) {
 // `greedy_ids` (device int64 [rows of logits], last stage only): also select
 // each row's greedy token, fused into lm_head where the decode GEMM runs it;
 // `out` may then be NULL when the logits themselves are not wanted.
+struct TopPSel {
+  float temperature, top_p;
+  const float* uniforms;  // [rows] in [0, 1)
+  int64_t* ids;           // [rows] out
+};
+
 int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64_t* ids,
               const void* hidden_in, const int64_t* positions, int out_mode, void* out,
-              cudaStream_t s, int64_t* greedy_ids = nullptr) {
+              cudaStream_t s, int64_t* greedy_ids = nullptr, const TopPSel* tp = nullptr) {
   const mg_stage_config& c = st->cfg;
   const int B = (int)rows.size();
   const int M = B * S;
@@ -547,6 +553,15 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   const int rows_out = last_only ? B : M;
   const bool fuse_greedy = greedy_ids && c.has_lm_head && !st->chain_enabled &&
                            gemv_tc_applicable(dt, rows_out, st->V, H);
+  // Top-p rows: the lm_head's epilogue counts the bf16 logits by value
+  // (kEpiHist) and one selection kernel draws from the histograms.
+  const bool fuse_hist = tp && c.has_lm_head && !st->chain_enabled && dt == kBF16 &&
+                         gemv_tc_applicable(dt, rows_out, st->V, H);
+  int* hist = nullptr;
+  if (tp && dt == kBF16) {
+    hist = top_p_hist_buffer(rows_out);
+    if (!hist) return fail(MG_ENOMEM, "top-p histogram buffer");
+  }
   if (greedy_ids && c.has_lm_head && !out && !fuse_greedy) {
     // the selection reads the logits: give them somewhere to go
     const size_t need = (size_t)rows_out * st->V * st->esz;
@@ -729,8 +744,10 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
                "final norm");
     la.M = rows_out;
     la.X = st->xn; la.ldx = H; la.W = st->lm_head; la.Y = out; la.ldy = st->V;
-    la.N = st->V; la.K = H; la.epilogue = fuse_greedy ? kEpiGreedy : kEpiStore; la.R = nullptr;
+    la.N = st->V; la.K = H; la.epilogue = fuse_greedy ? kEpiGreedy : fuse_hist ? kEpiHist : kEpiStore;
+    la.R = nullptr;
     if (fuse_greedy) la.greedy = Greedy{st->greedy_best, st->greedy_done, greedy_ids};
+    if (fuse_hist) la.hist = hist;
     MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "lm_head");
   } else {
     MG_CUDA(cudaMemcpyAsync(out, st->x, (size_t)M * H * st->esz, cudaMemcpyDeviceToDevice, s),
@@ -739,6 +756,22 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
   if (greedy_ids && c.has_lm_head && !fuse_greedy)
     MG_TIMED(MG_PROF_OTHER, (double)rows_out * st->V * st->esz, 0,
              launch_argmax(dt, out, rows_out, st->V, st->V, greedy_ids, s), "greedy selection");
+  if (tp && c.has_lm_head) {
+    const double row_bytes = (double)rows_out * st->V * st->esz;
+    if (dt != kBF16) {
+      MG_TIMED(MG_PROF_OTHER, row_bytes, 0,
+               launch_top_p(dt, out, rows_out, st->V, st->V, tp->temperature, tp->top_p, tp->uniforms, tp->ids, s),
+               "top-p selection");
+    } else {
+      if (!fuse_hist)
+        MG_TIMED(MG_PROF_OTHER, row_bytes, 0, launch_logit_hist(out, rows_out, st->V, st->V, hist, s),
+                 "top-p histogram");
+      MG_TIMED(MG_PROF_OTHER, row_bytes + (double)rows_out * kHistBins * 8, 0,
+               launch_top_p_select(out, rows_out, st->V, st->V, hist, tp->temperature, tp->top_p,
+                                   tp->uniforms, tp->ids, s),
+               "top-p selection");
+    }
+  }
   return MG_OK;
 }
 
@@ -1070,7 +1103,8 @@ int mg_stage_forward(mg_stage* st, int32_t slot, const int64_t* ids, const void*
 namespace {
 
 int decode_slots(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
-                 const void* hidden_in, int32_t out_mode, void* out, int64_t* greedy_ids, void* stream) {
+                 const void* hidden_in, int32_t out_mode, void* out, int64_t* greedy_ids, void* stream,
+                 const TopPSel* tp = nullptr) {
   int rc = check_inputs(st, ids, hidden_in);
   if (rc) return rc;
   rc = check_out_mode(st, out_mode);
@@ -1097,7 +1131,7 @@ int decode_slots(mg_stage* st, const int32_t* slots, int32_t n_slots, const int6
     for (int b = 0; b < sl.batch; ++b)
       rows.push_back(RowDesc{(uint64_t)sl.kv, (uint64_t)sl.tmap, sl.batch, b, sl.cap, sl.len});
   }
-  rc = run_stage(st, rows, 1, ids, hidden_in, nullptr, out_mode, out, s, greedy_ids);
+  rc = run_stage(st, rows, 1, ids, hidden_in, nullptr, out_mode, out, s, greedy_ids, tp);
   if (rc) return rc;
   for (int i = 0; i < n_slots; ++i) st->slots[slots[i]].len += 1;
   return MG_OK;
@@ -1151,6 +1185,20 @@ int mg_stage_probe_wait(mg_stage* st, uint32_t limit_us, int32_t flag_set, void*
   MG_LAUNCH(launch_wait_probe(flag, (uint64_t)limit_us * 1000ull, st->err, s), "wait probe");
   MG_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s), "probe flag reset");
   return MG_OK;
+}
+
+int mg_stage_decode_top_p(mg_stage* st, const int32_t* slots, int32_t n_slots, const int64_t* ids,
+                          const void* hidden_in, float temperature, float top_p, const float* uniforms,
+                          int64_t* ids_out, void* logits_out, void* stream) {
+  if (!st || !slots || n_slots < 1 || !ids_out || !logits_out)
+    return fail(MG_EINVAL, "null or empty argument");
+  if (!st->cfg.has_lm_head) return fail(MG_EINVAL, "top-p selection needs the last stage (lm_head)");
+  if (!(temperature > 0.f) || temperature != temperature || temperature > 3.4e38f)
+    return fail(MG_EINVAL, "temperature must be a finite positive number");
+  if (!(top_p >= 0.f && top_p <= 1.f)) return fail(MG_EINVAL, "top_p must be a finite number in [0, 1]");
+  if (!uniforms) return fail(MG_EINVAL, "uniforms are required");
+  const TopPSel tp{temperature, top_p, uniforms, ids_out};
+  return decode_slots(st, slots, n_slots, ids, hidden_in, MG_OUT_LOGITS_ALL, logits_out, nullptr, stream, &tp);
 }
 
 int mg_stage_check_device(mg_stage* st, void* stream) {

@@ -117,6 +117,20 @@ __device__ __forceinline__ void flag_error(int* err, int code) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Histogram bin of a logit (top-p by value histogram): the order-preserving
+// 16-bit key of its bf16 value, -0 counted as +0 so equal values share a bin.
+__device__ __forceinline__ uint32_t hist_bin(float v) {
+  uint32_t u = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  if ((u & 0x7fffu) == 0u) u = 0u;
+  return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u);
+}
+
+// The bf16 value of histogram bin `b` (the inverse of hist_bin).
+__device__ __forceinline__ float hist_value(uint32_t b) {
+  const uint32_t u = (b & 0x8000u) ? (b & 0x7fffu) : (~b & 0xffffu);
+  return __uint_as_float(u << 16);
+}
+
 // Streaming multiprocessors a persistent kernel spreads over on the current
 // device: the device's count minus the SMs left free for concurrent work
 // (NCCL's kernels in a multi-process pipeline; mg_reserve_sms).  Host code.

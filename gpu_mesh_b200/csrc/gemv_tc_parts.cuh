@@ -133,6 +133,17 @@ __device__ __forceinline__ unsigned long long greedy_key(float v, int index) {
   return ((unsigned long long)ord << 32) | (uint32_t)(0xffffffffu - (uint32_t)index);
 }
 
+// Count the finished logits of W row r of tile t (every token) into the
+// per-token value histograms (kEpiHist).
+template <int NP>
+__device__ __forceinline__ void hist_fold(const LinearArgs& a, int t, int r, const float* v) {
+  const int f = t * kRows + r;
+  if (f >= a.N) return;
+#pragma unroll
+  for (int tok = 0; tok < NP; ++tok)
+    if (tok < a.M) atomicAdd(a.hist + (size_t)tok * kHistBins + hist_bin(v[tok]), 1);
+}
+
 // Fold the finished logits of W row r of tile t (all tokens) into the
 // per-token maxima: a transposing butterfly leaves lane l holding the warp's
 // best key of token l (l < NP), then one atomic max per token and warp.

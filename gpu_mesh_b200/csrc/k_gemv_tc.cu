@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       if (!whole && !piece_done<NP>(p, slots, counters, c, t, r, e, v)) continue;  // another CTA finishes it
       apply<NP, EPI>(a, t, r, v, xchg);
       if (EPI == kEpiGreedy) greedy_fold<NP>(a, t, r, lane, v);
+      if (EPI == kEpiHist) hist_fold<NP>(a, t, r, v);
     }
     if (EPI == kEpiGreedy && ok) greedy_finish(a, e);
     if (!ok) *abort_flag = 1;
@@ -290,6 +291,9 @@ cudaError_t launch_gemv_tc(const LinearArgs& a, cudaStream_t s) {
     case kEpiGreedy:
       if (!a.greedy.best || !a.greedy.done || !a.greedy.ids) return cudaErrorInvalidValue;
       return launch_np<kEpiGreedy>(a, s);
+    case kEpiHist:
+      if (!a.hist || !a.Y) return cudaErrorInvalidValue;
+      return launch_np<kEpiHist>(a, s);
     default: return launch_np<kEpiSwiGLU>(a, s);
   }
 }

@@ -351,7 +351,8 @@ size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue) {
 cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s) {
   if (a.M == 0) return cudaSuccess;
   if (gemv_tc_applicable(a.dtype, a.M, a.N, a.K)) return launch_gemv_tc(a, s);
-  if (a.epilogue == kEpiPieces || a.epilogue == kEpiGreedy) return cudaErrorInvalidValue;  // decode GEMM only
+  if (a.epilogue == kEpiPieces || a.epilogue == kEpiGreedy || a.epilogue == kEpiHist)
+    return cudaErrorInvalidValue;  // decode GEMM only
   if (gemv_applicable(a.dtype, a.M, a.N, a.K)) {
     GemvPlan p = gemv_plan(a.M, a.N, a.K, a.epilogue);
     if (p.ksplit > 1 &&

@@ -17,6 +17,8 @@
 // input (one per row), so a seeded caller gets reproducible tokens.
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -280,7 +282,275 @@ __global__ void __launch_bounds__(kSampleThreads) top_p_kernel(const T* __restri
   if (threadIdx.x == 0) ids[blockIdx.x] = found >= 0 ? found : 0;
 }
 
+// ---------------------------------------------------------------------------
+// Top-p over bf16 logits by value histogram.
+//
+// Every token of one bf16 value has the same probability, so a row's
+// histogram of values (65536 bins, hist_bin order = value order) holds the
+// whole sorted distribution, tie groups included: the sort of
+// top_p_sample becomes a scan over the bins from the largest value down.
+// The histogram comes from the lm_head's epilogue (kEpiHist) or from
+// logit_hist_kernel.  top_p_select_kernel, one CTA per row, then
+//   1. finds the largest value present (m) and the softmax denominator
+//      Z0 = sum over bins of count * exp(v / T - m / T),
+//   2. gives each bin its probability p = exp(v / T - m / T) / Z0 and the
+//      mass of the bins above it (gt), and keeps
+//      min(count, floor((top_p - gt) / p) + 1) of its tokens when
+//      gt <= top_p (the reference keeps a token while the mass before it is
+//      <= top_p: sampling.py:85-88),
+//   3. draws x = u * (kept mass) and finds the bin and the rank inside it
+//      where the kept mass first exceeds x,
+//   4. clears its histogram for the next launch and returns the token of
+//      that rank among the row's indices of that value (index order, the
+//      stable sort's tie order).
+// Sums run in one fixed order (bins in order within a warp's slab, a fixed
+// butterfly across its lanes, warps in order), so a seeded draw is
+// reproducible.
+// ---------------------------------------------------------------------------
+
+constexpr int kSelThreads = 1024;
+constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kWarpBins = kHistBins / kSelWarps;  // 2048 bins per warp
+constexpr int kSlabs = kWarpBins / 32;            // 64 slabs of 32 bins
+
+__global__ void logit_hist_kernel(const __nv_bfloat16* __restrict__ logits, int vocab, int64_t stride,
+                                  int* __restrict__ hist) {
+  pdl_trigger();
+  pdl_wait();
+  const __nv_bfloat16* row = logits + (size_t)blockIdx.y * stride;
+  int* h = hist + (size_t)blockIdx.y * kHistBins;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x)
+    atomicAdd(h + hist_bin(__bfloat162float(row[i])), 1);
+}
+
+__device__ __forceinline__ float warp_incl_scan(float v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kSelThreads) top_p_select_kernel(
+    const __nv_bfloat16* __restrict__ logits, int vocab, int64_t stride, int* __restrict__ hist,
+    float temperature, float top_p, const float* __restrict__ uniforms, int64_t* __restrict__ ids) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float wsum[kSelWarps];
+  __shared__ float wkept[kSelWarps];
+  __shared__ int wfirst[kSelWarps];
+  __shared__ int cnt_s[kSelWarps];
+  __shared__ int sel_bin, sel_rank, found;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* h = hist + (size_t)blockIdx.x * kHistBins;
+  const __nv_bfloat16* row = logits + (size_t)blockIdx.x * stride;
+  // warp w, slab k, lane l: the bin at descending position w·2048 + k·32 + l
+  auto bin_at = [&](int k) { return (uint32_t)(kHistBins - 1 - (warp * kWarpBins + k * 32 + lane)); };
+  auto count_at = [&](uint32_t b) {
+    const int c = __ldcg(h + b);
+    const float v = hist_value(b);
+    return (v == v) ? c : 0;  // NaN logits take no part
+  };
+
+  // 1. The largest value present, and the denominator.
+  int first = INT_MAX;
+  for (int k = 0; k < kSlabs; ++k) {
+    const unsigned m = __ballot_sync(0xffffffffu, count_at(bin_at(k)) > 0);
+    if (m) {
+      first = warp * kWarpBins + k * 32 + __ffs(m) - 1;
+      break;
+    }
+  }
+  if (lane == 0) wfirst[warp] = first;
+  if (threadIdx.x == 0) {
+    sel_bin = -1;
+    sel_rank = 0;
+    found = -1;
+  }
+  __syncthreads();
+  int dmax = INT_MAX;
+  for (int i = 0; i < kSelWarps; ++i) dmax = min(dmax, wfirst[i]);
+  const float ms = dmax == INT_MAX ? 0.f : hist_value((uint32_t)(kHistBins - 1 - dmax)) / temperature;
+  float acc = 0.f;
+  for (int k = 0; k < kSlabs; ++k) {
+    const uint32_t b = bin_at(k);
+    const int c = count_at(b);
+    acc += warp_sum(c > 0 ? (float)c * expf(hist_value(b) / temperature - ms) : 0.f);
+  }
+  if (lane == 0) wsum[warp] = acc;
+  __syncthreads();
+  float z0 = 0.f;
+  for (int i = 0; i < kSelWarps; ++i) z0 += wsum[i];
+  __syncthreads();
+
+  // 2. The mass above each warp's bins, then each bin's kept count.
+  auto prob = [&](uint32_t b) { return expf(hist_value(b) / temperature - ms) / z0; };
+  acc = 0.f;
+  for (int k = 0; k < kSlabs; ++k) {
+    const uint32_t b = bin_at(k);
+    const int c = count_at(b);
+    acc += warp_sum(c > 0 ? (float)c * prob(b) : 0.f);
+  }
+  if (lane == 0) wsum[warp] = acc;
+  __syncthreads();
+  float above = 0.f;  // mass of the bins before this warp's range
+  for (int i = 0; i < warp; ++i) above += wsum[i];
+  // Walk this warp's slabs; `visit(k, gt, c, p, kept)` sees each bin.
+  auto walk = [&](auto&& visit) {
+    float carry = above;
+    for (int k = 0; k < kSlabs; ++k) {
+      const uint32_t b = bin_at(k);
+      const int c = count_at(b);
+      const float p = c > 0 ? prob(b) : 0.f;
+      const float mass = (float)c * p;
+      const float incl = warp_incl_scan(mass, lane);
+      const float gt = carry + (incl - mass);
+      int kept = 0;
+      if (c > 0 && gt <= top_p) kept = p > 0.f ? (int)fminf((float)c, floorf((top_p - gt) / p) + 1.0f) : c;
+      if (!visit(k, b, c, p, kept)) return;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  };
+  float kacc = 0.f;
+  walk([&](int, uint32_t, int, float p, int kept) {
+    kacc += warp_sum((float)kept * p);
+    return true;
+  });
+  if (lane == 0) wkept[warp] = kacc;
+  __syncthreads();
+  float ztot = 0.f, before = 0.f;
+  for (int i = 0; i < kSelWarps; ++i) {
+    if (i < warp) before += wkept[i];
+    ztot += wkept[i];
+  }
+  const float x = uniforms[blockIdx.x] * ztot;
+  // The drawing warp: the first whose kept mass reaches past x (or the last
+  // with any kept mass, when rounding puts x at the very end).
+  int target = -1, last_nonzero = -1;
+  {
+    float run = 0.f;
+    for (int i = 0; i < kSelWarps; ++i) {
+      if (wkept[i] > 0.f) last_nonzero = i;
+      if (target < 0 && wkept[i] > 0.f && run + wkept[i] > x) target = i;
+      run += wkept[i];
+    }
+    if (target < 0) target = last_nonzero;
+  }
+
+  // 3. The drawn bin and the rank inside it.
+  if (warp == target) {
+    float kcarry = before;
+    int last_b = -1, last_k = 0;
+    walk([&](int, uint32_t b, int, float p, int kept) {
+      const float km = (float)kept * p;
+      const float kincl = warp_incl_scan(km, lane);
+      const unsigned hit = __ballot_sync(0xffffffffu, kept > 0 && kcarry + kincl > x);
+      const unsigned any = __ballot_sync(0xffffffffu, kept > 0);
+      if (any) {
+        const int hl = 31 - __clz(any);
+        last_b = __shfl_sync(0xffffffffu, (int)b, hl);
+        last_k = __shfl_sync(0xffffffffu, kept, hl);
+      }
+      if (hit) {
+        const int l = __ffs(hit) - 1;
+        if (lane == l) {
+          const float lo = kcarry + (kincl - km);
+          int rank = p > 0.f ? (int)floorf((x - lo) / p) : 0;
+          rank = max(0, min(rank, kept - 1));
+          sel_bin = (int)b;
+          sel_rank = rank;
+        }
+        return false;
+      }
+      kcarry += __shfl_sync(0xffffffffu, kincl, 31);
+      return true;
+    });
+    if (lane == 0 && sel_bin < 0 && last_b >= 0) {  // x at the very end of the kept mass
+      sel_bin = last_b;
+      sel_rank = last_k - 1;
+    }
+  }
+  __syncthreads();
+
+  // 4. Clear the histogram; find the token of that rank.
+  for (int k = 0; k < kSlabs; ++k) h[bin_at(k)] = 0;
+  if (sel_bin < 0) {  // no finite logits
+    if (threadIdx.x == 0) ids[blockIdx.x] = 0;
+    return;
+  }
+  const float wv = hist_value((uint32_t)sel_bin);
+  const int run = (vocab + kSelThreads - 1) / kSelThreads;
+  const int i0 = threadIdx.x * run, i1 = min(vocab, i0 + run);
+  int mine = 0;
+  for (int i = i0; i < i1; ++i) mine += __bfloat162float(row[i]) == wv;
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) cnt_s[warp] = incl;
+  __syncthreads();
+  int prior = incl - mine;
+  for (int k = 0; k < warp; ++k) prior += cnt_s[k];
+  const int rank = sel_rank;
+  if (mine > 0 && rank >= prior && rank < prior + mine) {
+    int k = prior;
+    for (int i = i0; i < i1; ++i)
+      if (__bfloat162float(row[i]) == wv) {
+        if (k == rank) {
+          found = i;
+          break;
+        }
+        ++k;
+      }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ids[blockIdx.x] = found >= 0 ? found : 0;
+}
+
 }  // namespace
+
+int* top_p_hist_buffer(int rows) {
+  static int* buf[64] = {};
+  static size_t cap[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || rows < 0) return nullptr;
+  const size_t need = (size_t)(rows > 0 ? rows : 1) * kHistBins;
+  if (need > cap[dev]) {
+    if (buf[dev]) {
+      cudaDeviceSynchronize();
+      cudaFree(buf[dev]);
+      buf[dev] = nullptr;
+      cap[dev] = 0;
+    }
+    if (cudaMalloc(&buf[dev], need * sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(buf[dev], 0, need * sizeof(int)) != cudaSuccess) return nullptr;
+    cap[dev] = need;
+  }
+  return buf[dev];
+}
+
+cudaError_t launch_logit_hist(const void* logits, int rows, int vocab, int64_t stride, int* hist,
+                              cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int blocks = std::min(64, (vocab + 255) / 256);
+  const cudaError_t e = launch_pdl(logit_hist_kernel, dim3(blocks, rows), dim3(256), 0, s,
+                                   (const __nv_bfloat16*)logits, vocab, stride, hist);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_top_p_select(const void* logits, int rows, int vocab, int64_t stride, int* hist,
+                                float temperature, float top_p, const float* uniforms, int64_t* ids,
+                                cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const cudaError_t e = launch_pdl(top_p_select_kernel, dim3(rows), dim3(kSelThreads), 0, s,
+                                   (const __nv_bfloat16*)logits, vocab, stride, hist, temperature, top_p,
+                                   uniforms, ids);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
 
 cudaError_t launch_argmax(int dtype, const void* logits, int rows, int vocab, int64_t stride,
                           int64_t* ids, cudaStream_t s) {
@@ -298,7 +568,14 @@ cudaError_t launch_top_p(int dtype, const void* logits, int rows, int vocab, int
                          cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   if (!(temperature > 0.f)) return launch_argmax(dtype, logits, rows, vocab, stride, ids, s);
-  // The rows' probabilities: a per-device scratch buffer, grown on demand
+  if (dtype == kBF16) {  // by value histogram (see top_p_select_kernel)
+    int* hist = top_p_hist_buffer(rows);
+    if (!hist) return cudaErrorMemoryAllocation;
+    cudaError_t e = launch_logit_hist(logits, rows, vocab, stride, hist, s);
+    if (e != cudaSuccess) return e;
+    return launch_top_p_select(logits, rows, vocab, stride, hist, temperature, top_p, uniforms, ids, s);
+  }
+  // fp32 logits: the rows' probabilities: a per-device scratch buffer, grown on demand
   // (the growth synchronises the device once).
   static float* scratch[64] = {};
   static size_t scratch_elems[64] = {};

@@ -72,6 +72,7 @@ enum Epilogue : int {
   kEpiSwiGLU = 2,  // Y[:, n] = round(round(silu(round(acc_gate))) * round(acc_up))
   kEpiPieces = 3,  // decode GEMM only: every CTA's fp32 sums left as pieces (see Pieces)
   kEpiGreedy = 4,  // decode GEMM only (lm_head): kEpiStore (Y may be NULL) + per-row argmax (see Greedy)
+  kEpiHist = 5,    // decode GEMM only (lm_head): kEpiStore + per-row histogram of the bf16 logits (top-p)
 };
 
 // Greedy selection fused into the lm_head decode GEMM.  Every CTA folds the
@@ -187,7 +188,30 @@ struct LinearArgs {
   size_t counters_elems;
   // kEpiGreedy: the selection buffers (device pointers; unused otherwise).
   Greedy greedy{nullptr, nullptr, nullptr};
+  // kEpiHist: [M][kHistBins] counts of each row's logits by bf16 value, zero
+  // when the launch starts (launch_top_p_select clears what it reads).
+  int* hist = nullptr;
 };
+
+// Top-p over bf16 logits by value histogram: a bf16 logit has one of 65536
+// bit patterns, and every token of one value has the same probability, so a
+// row's histogram of values holds its whole sorted distribution.
+constexpr int kHistBins = 65536;
+
+// A zeroed [rows][kHistBins] int buffer of the current device, grown on
+// demand (growth synchronises the device once); NULL on allocation failure.
+int* top_p_hist_buffer(int rows);
+
+// Count each bf16 logit of `rows` rows into hist (the histogram half of
+// launch_top_p, for logits that were not counted by the lm_head epilogue).
+cudaError_t launch_logit_hist(const void* logits, int rows, int vocab, int64_t row_stride, int* hist,
+                              cudaStream_t s);
+
+// From each row's histogram and bf16 logits: the top-p token for uniform
+// uniforms[r] (the rule of launch_top_p), into ids; clears the histograms.
+cudaError_t launch_top_p_select(const void* logits, int rows, int vocab, int64_t row_stride, int* hist,
+                                float temperature, float top_p, const float* uniforms, int64_t* ids,
+                                cudaStream_t s);
 
 // Scratch (fp32 elements) that launch_linear needs for the given shape.
 size_t linear_scratch_elems(int dtype, int M, int N, int K, int epilogue);

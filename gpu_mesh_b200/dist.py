@@ -226,12 +226,18 @@ class PipelineRank:
         returns the last step's ids per group on rank 0."""
         st = self.stage
         greedy_inside = self.ring.last and self.top_p is None
+        top_p_inside = self.ring.last and self.top_p is not None
 
         def forward(k, g, x):
             slot = [self.slots[g]]
             if greedy_inside:
                 return st.decode_greedy(slot, None if self.ring.first else x,
                                         input_ids=x if self.ring.first else None)[0]
+            if top_p_inside:  # drawn from the histograms counted in the lm_head's epilogue
+                u = torch.rand(self.rows, generator=self.sample_gen, device=self.device)
+                return st.decode_top_p(slot, None if self.ring.first else x, temperature=self.top_p[0],
+                                       top_p=self.top_p[1], uniforms=u,
+                                       input_ids=x if self.ring.first else None)[0]
             if self.ring.first:
                 return st.decode_multi(slot, None, input_ids=x, logits="last")
             return st.decode_multi(slot, x, logits="last")

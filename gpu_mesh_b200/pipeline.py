@@ -443,6 +443,38 @@ def pipeline_decode_greedy(
     return _run_plan(_multi_plan(workers, next_tokens, cache_keys, "pipeline_decode_greedy", last))
 
 
+@torch.no_grad()
+def pipeline_decode_top_p(
+    workers: list[B200StageWorker],
+    next_tokens: torch.Tensor,
+    *,
+    cache_keys: Sequence[str | None],
+    temperature: float,
+    top_p: float,
+    generator: torch.Generator | None = None,
+    uniforms: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``pipeline_decode_multi`` whose last stage also draws every row's
+    top-p token on the device (counted in its lm_head): returns (token ids
+    int64 [rows], logits [rows, 1, V]).  The draw of row r is ``uniforms[r]``
+    (default: ``torch.rand`` with ``generator``), as ``top_p_sample`` draws
+    (inference/sampling.py:63-95; the reference hands the nucleus to
+    ``torch.multinomial``).  Temperature 0 is greedy, as the reference's."""
+    if temperature <= 0:
+        ids, logits = pipeline_decode_greedy(workers, next_tokens, cache_keys=cache_keys, return_logits=True)
+        return ids, logits
+    rows = next_tokens.shape[0]
+    if uniforms is None:
+        dev = generator.device if generator is not None else torch.device("cpu")
+        uniforms = torch.rand(rows, generator=generator, device=dev)
+
+    def last(worker, hidden, keys, ids):
+        return _Call(worker, "decode_top_p", (hidden, keys),
+                     dict(input_ids=ids, temperature=temperature, top_p=top_p, uniforms=uniforms))
+
+    return _run_plan(_multi_plan(workers, next_tokens, cache_keys, "pipeline_decode_top_p", last))
+
+
 async def pipeline_prefill_async(
     workers: list[Any],
     input_ids: torch.Tensor,
@@ -481,6 +513,7 @@ __all__ = [
     "pipeline_decode_step",
     "pipeline_decode_multi",
     "pipeline_decode_greedy",
+    "pipeline_decode_top_p",
     "pipeline_prefill_async",
     "pipeline_decode_step_async",
 ]

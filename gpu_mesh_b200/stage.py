@@ -463,6 +463,47 @@ class B200Stage:
         )
         return tokens, logits
 
+    def decode_top_p(
+        self,
+        slots: list[int],
+        x: torch.Tensor | None,
+        *,
+        temperature: float,
+        top_p: float,
+        uniforms: torch.Tensor,
+        input_ids: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """``decode_multi`` on the last stage with each row's top-p token drawn
+        on the device for ``uniforms[r]`` (the selection counts the logits by
+        value in the lm_head's epilogue).  Returns (token ids int64 [rows],
+        logits [rows, 1, V])."""
+        if not self.has_lm_head:
+            raise ValueError("decode_top_p runs on the last stage")
+        rows = sum(self.kv_batch(s) for s in slots)
+        arr = (ctypes.c_int32 * len(slots))(*slots)
+        ids = None
+        if self.has_embedding:
+            if input_ids is None or input_ids.shape[0] != rows:
+                raise ValueError(f"decode_top_p needs input_ids with {rows} rows")
+            ids = input_ids.to(device=self.device, dtype=torch.int64).contiguous()
+        else:
+            if x is None or x.shape[0] != rows or x.shape[-1] != self.cfg.hidden_size:
+                raise ValueError(f"decode_top_p needs hidden states with {rows} rows")
+            x = x.to(self.device).contiguous()
+        u = uniforms.to(device=self.device, dtype=torch.float32).reshape(-1).contiguous()
+        if u.numel() != rows:
+            raise ValueError(f"decode_top_p needs one uniform per row ({rows})")
+        tokens = torch.empty(rows, dtype=torch.int64, device=self.device)
+        logits = torch.empty((rows, 1, self.cfg.vocab_size), dtype=self.dtype, device=self.device)
+        _lib.check(
+            self._lib.mg_stage_decode_top_p(
+                self.handle, arr, len(slots), _ptr(ids), None if self.has_embedding else _ptr(x),
+                float(temperature), float(top_p), u.data_ptr(), tokens.data_ptr(), logits.data_ptr(),
+                _stream(self.device),
+            )
+        )
+        return tokens, logits
+
     def profile(self, enable: bool) -> None:
         """Time every launch group with CUDA events (resets on enable)."""
         _lib.check(self._lib.mg_stage_profile(self.handle, int(enable)))

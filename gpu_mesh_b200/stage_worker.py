@@ -192,6 +192,27 @@ class B200StageWorker:
                                                        return_logits=return_logits)
         return self._boundary_output(tokens), (None if logits is None else self._boundary_output(logits))
 
+    def decode_top_p(
+        self,
+        hidden: torch.Tensor | None,
+        cache_keys: list[str | None],
+        *,
+        temperature: float,
+        top_p: float,
+        uniforms: torch.Tensor,
+        input_ids: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """``decode_multi`` on the last stage returning each row's top-p token
+        for ``uniforms`` (drawn on the device) and the logits."""
+        with self._inference_lock:
+            slots = [self._slot(k) for k in cache_keys]
+            x = None
+            if hidden is not None:
+                x = self._move_input(hidden)
+            tokens, logits = self._model.decode_top_p(slots, x, temperature=temperature, top_p=top_p,
+                                                      uniforms=uniforms, input_ids=input_ids)
+        return self._boundary_output(tokens), self._boundary_output(logits)
+
     # ------------------------------------------------------------------
     # KV ownership (stage_worker.py:358-416)
     # ------------------------------------------------------------------

@@ -231,6 +231,17 @@ int mg_stage_decode_greedy(mg_stage* stage, const int32_t* slots, int32_t n_slot
                            const int64_t* input_ids, const void* hidden_in, int64_t* ids_out,
                            void* logits_out, void* stream);
 
+/* mg_stage_decode_multi on the last stage plus top_p_sample of every row
+ * (inference/sampling.py:63-95) with temperature > 0: the lm_head's epilogue
+ * counts each row's bf16 logits by value into a histogram, and one selection
+ * kernel draws the token for uniforms[r] by the rule of mg_sample_top_p
+ * (the same token, up to the rounding of the cumulative sums).  The logits
+ * [rows, V] are also written to `logits_out` (the selection reads them).
+ * fp32 stages sample the written logits with mg_sample_top_p's kernel. */
+int mg_stage_decode_top_p(mg_stage* stage, const int32_t* slots, int32_t n_slots, const int64_t* input_ids,
+                          const void* hidden_in, float temperature, float top_p, const float* uniforms,
+                          int64_t* ids_out, void* logits_out, void* stream);
+
 /* Read and clear the stage's device error word (waits for `stream`).
  * Returns MG_EDEVICE with a message when a kernel met an out-of-range token
  * id or position since the last check. */
