@@ -7,10 +7,13 @@ on another implementation.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmeshgpu_b200.so"
+# MESHGPU_LIB names a build of the library made elsewhere (for example with other
+# compile-time tuning macros); by default the in-tree build is loaded.
+LIB_PATH = Path(os.environ.get("MESHGPU_LIB") or Path(__file__).resolve().parent / "lib" / "libmeshgpu_b200.so")
 
 MG_OK = 0
 MG_EINVAL = 1

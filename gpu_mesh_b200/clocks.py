@@ -1,7 +1,10 @@
 """GPU clock and throttle-reason sampling during a timed region.
 
-``nvidia-smi`` polls the GPU in a child process; a reader thread stamps each
-line with the host clock.  Entering the context waits (up to a few seconds)
+Where NVML answers (``pynvml``), a thread reads the SM clock, the maximum
+clock and the active clock-event reasons every 5 ms, so a timed region of a
+hundred milliseconds carries about twenty samples.  Otherwise ``nvidia-smi``
+polls the GPU in a child process and a reader thread stamps each line with
+the host clock.  Entering the context waits (up to a few seconds)
 for the first sample, so the poller is running before the timed region
 starts, and leaving it waits for one more sample, so a region shorter than
 the polling interval still has one.  The summary keeps only samples stamped
@@ -16,8 +19,58 @@ import threading
 import time
 
 
+class _NvmlPoller:
+    """Read-only NVML polling of one GPU in a thread; lines in nvidia-smi's CSV layout."""
+
+    PERIOD_S = 0.005
+
+    def __init__(self, gpu: int, sink) -> None:
+        import pynvml
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu)
+        self.gpu, self.sink = gpu, sink
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _line(self) -> str:
+        nv, h = self.nv, self.h
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        try:
+            power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+        except nv.NVMLError:
+            power = 0.0
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        # hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
+        order = (nv.nvmlClocksThrottleReasonHwSlowdown, nv.nvmlClocksThrottleReasonHwThermalSlowdown,
+                 nv.nvmlClocksThrottleReasonSwThermalSlowdown, nv.nvmlClocksThrottleReasonSwPowerCap)
+        flags = ["Active" if bits & b else "Not Active" for b in order]
+        return f"{self.gpu}, {sm}, {mx}, {power:.1f}, {bits:#x}, " + ", ".join(flags)
+
+    def _run(self) -> None:
+        while not self.stop.is_set():
+            try:
+                self.sink(self._line())
+            except Exception:
+                return
+            self.stop.wait(self.PERIOD_S)
+
+    def start(self) -> None:
+        self.thread.start()
+
+    def terminate(self) -> None:
+        self.stop.set()
+        self.thread.join(timeout=5)
+        try:
+            self.nv.nvmlShutdown()
+        except Exception:
+            pass
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """Clocks and throttle reasons sampled during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -28,6 +81,7 @@ class ClockSampler:
     def __init__(self, gpu: int) -> None:
         self.gpu = gpu
         self.proc = None
+        self.nvml = None
         self.samples: list[tuple[float, str]] = []
         self.t0 = self.t1 = 0.0
         self._cv = threading.Condition()
@@ -44,7 +98,21 @@ class ClockSampler:
         with self._cv:
             self._cv.wait_for(lambda: len(self.samples) >= count, timeout=timeout)
 
+    def _push(self, line: str) -> None:
+        with self._cv:
+            self.samples.append((time.monotonic(), line))
+            self._cv.notify_all()
+
     def __enter__(self):
+        self.nvml = None
+        try:
+            self.nvml = _NvmlPoller(self.gpu, self._push)
+            self.nvml.start()
+            self._wait_for(1, self.START_WAIT_S)
+            self.t0 = time.monotonic()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -62,6 +130,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         self.t1 = time.monotonic()
+        if self.nvml is not None:
+            self.nvml.terminate()
+            return
         if self.proc is None:
             return
         with self._cv:
