@@ -312,6 +312,7 @@ constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kWarpBins = kHistBins / kSelWarps;  // 2048 bins per warp
 constexpr int kSlabs = kWarpBins / 32;            // 64 slabs of 32 bins
+constexpr int kMaxCand = 4096;                    // tie-group indices gathered in shared memory
 
 __global__ void logit_hist_kernel(const __nv_bfloat16* __restrict__ logits, int vocab, int64_t stride,
                                   int* __restrict__ hist) {
@@ -341,14 +342,37 @@ __global__ void __launch_bounds__(kSelThreads) top_p_select_kernel(
   __shared__ float wkept[kSelWarps];
   __shared__ int wfirst[kSelWarps];
   __shared__ int cnt_s[kSelWarps];
-  __shared__ int sel_bin, sel_rank, found;
+  __shared__ int sel_bin, sel_rank, found, n_cand, wide;
+  __shared__ int cand[kMaxCand];
+  // The row's counts, staged once into shared memory as 16-bit values (the
+  // passes below then read shared memory, not L2); a row with a count of
+  // 65535 or more in one bin reads its counts from the histogram instead.
+  extern __shared__ uint16_t c16[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* h = hist + (size_t)blockIdx.x * kHistBins;
   const __nv_bfloat16* row = logits + (size_t)blockIdx.x * stride;
+  if (threadIdx.x == 0) wide = 0;
+  __syncthreads();
+  {
+    int big = 0;
+    const int4* h4 = reinterpret_cast<const int4*>(h);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < kHistBins / 4; i += kSelThreads) {
+      const int4 q = __ldcg(h4 + i);
+      big |= (q.x >= 0xffff) | (q.y >= 0xffff) | (q.z >= 0xffff) | (q.w >= 0xffff);
+      c16[4 * i] = (uint16_t)min(q.x, 0xffff);
+      c16[4 * i + 1] = (uint16_t)min(q.y, 0xffff);
+      c16[4 * i + 2] = (uint16_t)min(q.z, 0xffff);
+      c16[4 * i + 3] = (uint16_t)min(q.w, 0xffff);
+    }
+    if (big) wide = 1;
+  }
+  __syncthreads();
+  const bool from_l2 = wide != 0;
   // warp w, slab k, lane l: the bin at descending position w·2048 + k·32 + l
   auto bin_at = [&](int k) { return (uint32_t)(kHistBins - 1 - (warp * kWarpBins + k * 32 + lane)); };
   auto count_at = [&](uint32_t b) {
-    const int c = __ldcg(h + b);
+    const int c = from_l2 ? __ldcg(h + b) : (int)c16[b];
     const float v = hist_value(b);
     return (v == v) ? c : 0;  // NaN logits take no part
   };
@@ -474,37 +498,76 @@ __global__ void __launch_bounds__(kSelThreads) top_p_select_kernel(
   __syncthreads();
 
   // 4. Clear the histogram; find the token of that rank.
-  for (int k = 0; k < kSlabs; ++k) h[bin_at(k)] = 0;
+  {
+    int4* h4 = reinterpret_cast<int4*>(h);
+    for (int i = threadIdx.x; i < kHistBins / 4; i += kSelThreads) h4[i] = make_int4(0, 0, 0, 0);
+  }
   if (sel_bin < 0) {  // no finite logits
     if (threadIdx.x == 0) ids[blockIdx.x] = 0;
     return;
   }
   const float wv = hist_value((uint32_t)sel_bin);
-  const int run = (vocab + kSelThreads - 1) / kSelThreads;
-  const int i0 = threadIdx.x * run, i1 = min(vocab, i0 + run);
-  int mine = 0;
-  for (int i = i0; i < i1; ++i) mine += __bfloat162float(row[i]) == wv;
-  int incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  if (lane == 31) cnt_s[warp] = incl;
-  __syncthreads();
-  int prior = incl - mine;
-  for (int k = 0; k < warp; ++k) prior += cnt_s[k];
   const int rank = sel_rank;
-  if (mine > 0 && rank >= prior && rank < prior + mine) {
-    int k = prior;
-    for (int i = i0; i < i1; ++i)
-      if (__bfloat162float(row[i]) == wv) {
-        if (k == rank) {
-          found = i;
-          break;
+  if (threadIdx.x == 0) n_cand = 0;
+  __syncthreads();
+  // The tie group's indices, gathered with coalesced loads (unordered); the
+  // token is the one with exactly `rank` smaller indices in the group.
+  auto take = [&](int i) {
+    const int slot = atomicAdd(&n_cand, 1);
+    if (slot < kMaxCand) cand[slot] = i;
+  };
+  if ((stride % 8) == 0 && ((uintptr_t)row % 16) == 0) {  // 16-byte loads of 8 logits
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    for (int g8 = threadIdx.x; g8 < vocab / 8; g8 += kSelThreads) {
+      const uint4 q = r4[g8];
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (__bfloat162float(e[j]) == wv) take(8 * g8 + j);
+    }
+    for (int i = vocab / 8 * 8 + threadIdx.x; i < vocab; i += kSelThreads)
+      if (__bfloat162float(row[i]) == wv) take(i);
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += kSelThreads)
+      if (__bfloat162float(row[i]) == wv) take(i);
+  }
+  __syncthreads();
+  const int nc = n_cand;
+  if (nc <= kMaxCand) {
+    for (int j = threadIdx.x; j < nc; j += kSelThreads) {
+      const int me = cand[j];
+      int smaller = 0;
+      for (int k = 0; k < nc; ++k) smaller += cand[k] < me;
+      if (smaller == rank) found = me;
+    }
+  } else {
+    // ordered runs: thread t counts its contiguous run, an exclusive scan
+    // over threads finds the run holding the rank, that thread walks it
+    const int run = (vocab + kSelThreads - 1) / kSelThreads;
+    const int i0 = threadIdx.x * run, i1 = min(vocab, i0 + run);
+    int mine = 0;
+    for (int i = i0; i < i1; ++i) mine += __bfloat162float(row[i]) == wv;
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) cnt_s[warp] = incl;
+    __syncthreads();
+    int prior = incl - mine;
+    for (int k = 0; k < warp; ++k) prior += cnt_s[k];
+    if (mine > 0 && rank >= prior && rank < prior + mine) {
+      int k = prior;
+      for (int i = i0; i < i1; ++i)
+        if (__bfloat162float(row[i]) == wv) {
+          if (k == rank) {
+            found = i;
+            break;
+          }
+          ++k;
         }
-        ++k;
-      }
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) ids[blockIdx.x] = found >= 0 ? found : 0;
@@ -546,7 +609,17 @@ cudaError_t launch_top_p_select(const void* logits, int rows, int vocab, int64_t
                                 float temperature, float top_p, const float* uniforms, int64_t* ids,
                                 cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  const cudaError_t e = launch_pdl(top_p_select_kernel, dim3(rows), dim3(kSelThreads), 0, s,
+  constexpr int smem = kHistBins * (int)sizeof(uint16_t);  // 128 KB of staged counts
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(top_p_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const cudaError_t e = launch_pdl(top_p_select_kernel, dim3(rows), dim3(kSelThreads), smem, s,
                                    (const __nv_bfloat16*)logits, vocab, stride, hist, temperature, top_p,
                                    uniforms, ids);
   return e != cudaSuccess ? e : cudaGetLastError();
