@@ -333,6 +333,46 @@ def long_context(hbm: float, *, rows: int = 64, context: int = 8192, layers: int
     }
 
 
+def prefill_attention_rate(worker, cfg, prompt) -> dict:
+    """Causal prefill attention of one micro-batch: this stage's tcgen05
+    kernel (every layer's launch bracketed by CUDA events during a prefill of
+    ``prompt`` into a scratch context) next to the library path the
+    reference would reach on this GPU, torch's scaled_dot_product_attention
+    (bf16, causal, GQA) on the same shape.  Reported only; the library is
+    not on the stage's path."""
+    stage = worker._model
+    B, S = prompt.shape
+    stage.profile(True)
+    worker.forward_inference(None, input_ids=prompt, operation_id=1, attempt_id="pa", cache_key="pa",
+                             logits="last")
+    att = stage.profile_read()["attention"]
+    stage.profile(False)
+    worker.clear_kv("pa")
+    ours = att["flops"] / (att["ms"] / 1000.0) / 1e12 if att["ms"] else None
+    nq, nkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    g = torch.Generator(device=prompt.device).manual_seed(9)
+    q = torch.randn(B, nq, S, D, generator=g, device=prompt.device, dtype=torch.bfloat16)
+    k = torch.randn(B, nkv, S, D, generator=g, device=prompt.device, dtype=torch.bfloat16)
+    v = torch.randn(B, nkv, S, D, generator=g, device=prompt.device, dtype=torch.bfloat16)
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    for _ in range(3):
+        sdpa(q, k, v, is_causal=True, enable_gqa=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        sdpa(q, k, v, is_causal=True, enable_gqa=True)
+    e1.record()
+    torch.cuda.synchronize()
+    flops = 4.0 * B * nq * D * (S * (S + 1) / 2)
+    lib = flops / (e0.elapsed_time(e1) / reps / 1000.0) / 1e12
+    return {"shape": f"{B} rows x {S} tokens, {nq} q / {nkv} KV heads, head_dim {D}, causal",
+            "b200_tflops": ours, "sdpa_tflops": lib, "unit": "TFLOP/s",
+            "note": "b200: attn_prefill_tc per layer, event-bracketed; sdpa: torch's default backend, "
+                    "reported for comparison only"}
+
+
 # ---------------------------------------------------------------------------
 # B200 arm, one GPU
 # ---------------------------------------------------------------------------
@@ -372,6 +412,7 @@ def run_single(args) -> None:
     prefill_ms = t0.elapsed_time(t1)
     stage.check_device()  # a kernel that gave up waiting would make every number below meaningless
     ids = torch.cat(first).unsqueeze(-1)
+    prefill_attention = prefill_attention_rate(w, cfg, prompts[0].to(dev))
 
     rows_all = args.micro * args.micro_batches
 
@@ -515,6 +556,7 @@ def run_single(args) -> None:
             / sustained_bf16_tflops(),
         },
         "gpu_launches": int(launches),
+        "prefill_attention": prefill_attention,
         "profile": prof,
         "clocks": clocks.summary(),
     }
