@@ -208,10 +208,10 @@ class PipelineRank:
         return decode_loop(self.ring, self.groups, n_steps, inputs, forward, sample,
                            lambda k, g: bufs[g], lambda g: self._ids[g], ret_group=self.ret_group)
 
-    def prefill(self, prompts: list[torch.Tensor] | None, *, host_tokens: bool = False):
-        """One prefill pass of every group's prompt [rows, S] (given on rank 0,
-        None elsewhere; every rank must know S through ``prompt_len``); returns
-        the first sampled ids per group on rank 0."""
+    def prefill(self, prompts: list[torch.Tensor] | None, prompt_len: int, *, host_tokens: bool = False):
+        """One prefill pass of every group's prompt [rows, prompt_len] (given on
+        rank 0, None elsewhere: the other ranks size their receive buffers from
+        ``prompt_len``); returns the first sampled ids per group on rank 0."""
         st = self.stage
 
         def forward(k, g, x):
@@ -219,7 +219,7 @@ class PipelineRank:
                 return st.forward_slot(self.slots[g], None, input_ids=x, logits="last", check_values=False)
             return st.forward_slot(self.slots[g], x, logits="last", check_values=False)
 
-        return self._run(1, prompts, forward, self.prompt_len, host_tokens)
+        return self._run(1, prompts, forward, prompt_len, host_tokens)
 
     def decode(self, ids: list[torch.Tensor] | None, n_steps: int, *, host_tokens: bool = False):
         """``n_steps`` decode steps of every group from ``ids`` (rank 0);
@@ -263,8 +263,6 @@ class PipelineRank:
 
     def close(self) -> None:
         self.stage.close()
-
-    prompt_len: int = 0
 
 
 def verify_one_gpu(cfg, prompts: list[torch.Tensor], record: list[tuple[int, torch.Tensor]], groups: int,
@@ -361,7 +359,6 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
         nccl_sms = getattr(args, "nccl_sms", 8)
         pr = PipelineRank(cfg, groups=n_groups, rows=rows, capacity=cap, layer_ranges=ranges, top_p=top_p,
                           nccl_sms=nccl_sms)
-        pr.prompt_len = args.prompt
         g = torch.Generator().manual_seed(1000)
         prompts_host = [torch.randint(0, cfg.vocab_size, (rows, args.prompt), generator=g)
                         for _ in range(n_groups)]
@@ -382,10 +379,10 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
 
         # One untimed prefill first (the communicators connect and every kernel
         # is configured on first use), then the caches are rolled back.
-        timed(lambda: pr.prefill(prompts))
+        timed(lambda: pr.prefill(prompts, args.prompt))
         pr.reset()
         pr.record = [] if top_p is None else None  # ids of every iteration, for the one-GPU check
-        ids, prefill_ms = timed(lambda: pr.prefill(prompts))
+        ids, prefill_ms = timed(lambda: pr.prefill(prompts, args.prompt))
         ids, _ = timed(lambda: pr.decode(ids, args.warmup))
         launches0 = _launches()
         with (ClockSampler(local) if ring.first else nullcontext()) as clocks:
@@ -409,11 +406,10 @@ def run_pipeline_bench(args, cfg, metric: str, workload: dict, peaks: tuple[floa
                         balanced_layer_ranges(cfg, world, rows=rows_total * n_groups, context=mean_ctx))
             pw = PipelineRank(cfg, groups=n_groups, rows=rows_total, capacity=cap, layer_ranges=ranges_w,
                               top_p=top_p, nccl_sms=nccl_sms)
-            pw.prompt_len = args.prompt
             gw = torch.Generator().manual_seed(2000)
             prompts_w = [torch.randint(0, cfg.vocab_size, (rows_total, args.prompt), generator=gw).to(dev)
                          for _ in range(n_groups)] if ring.first else None
-            idw, _ = timed(lambda: pw.prefill(prompts_w))
+            idw, _ = timed(lambda: pw.prefill(prompts_w, args.prompt))
             idw, _ = timed(lambda: pw.decode(idw, args.warmup))
             idw, ms_w = timed(lambda: pw.decode(idw, args.steps))
             pw.close()
@@ -549,10 +545,9 @@ def run_other_config(spec: dict, args, timed) -> dict:
             ids = ([torch.randint(0, cfg.vocab_size, (rows, 1), generator=g).to(dev) for _ in range(groups)]
                    if pr.ring.first else None)
         else:
-            pr.prompt_len = spec["prompt"]
             prompts = ([torch.randint(0, cfg.vocab_size, (rows, spec["prompt"]), generator=g).to(dev)
                         for _ in range(groups)] if pr.ring.first else None)
-            ids, pf_ms = timed(lambda: pr.prefill(prompts))
+            ids, pf_ms = timed(lambda: pr.prefill(prompts, spec["prompt"]))
             out["prefill_tok_s"] = rows_total * spec["prompt"] / (pf_ms / 1000.0)
         ids, _ = timed(lambda: pr.decode(ids, args.warmup))
         ids, ms = timed(lambda: pr.decode(ids, args.steps))
