@@ -325,3 +325,24 @@ def top_p_acceptable(logits: torch.Tensor, temperature: float, top_p: float, u: 
         hit = (inc > u - eps) & (exc <= u + eps)
         out.update(si[:n][hit].tolist())
     return out
+
+
+def exact_bar(got: torch.Tensor, ref: torch.Tensor, exact: torch.Tensor, what: str = "") -> dict:
+    """The bf16 parity bar at full model width, where north of 2e-2 max-abs is
+    the reference's own rounding noise: the implementation under test must be
+    no further from the exactly-rounded computation (``exact_rounding``) than
+    the reference's bf16 arithmetic (this oracle, or the reference itself) is:
+
+        mean |got - exact| <= 1.5 * mean |ref - exact| + 1e-3
+        max  |got - exact| <= max(2e-2, 2 * max |ref - exact|)
+
+    Raises AssertionError with the figures; returns them otherwise."""
+    e_got, e_ref = (got.float() - exact.float()).abs(), (ref.float() - exact.float()).abs()
+    stats = {
+        "mean_got": float(e_got.mean()), "mean_ref": float(e_ref.mean()),
+        "max_got": float(e_got.max()), "max_ref": float(e_ref.max()),
+        "max_got_vs_ref": float((got.float() - ref.float()).abs().max()),
+    }
+    assert stats["mean_got"] <= 1.5 * stats["mean_ref"] + 1e-3, (what, stats)
+    assert stats["max_got"] <= max(2e-2, 2 * stats["max_ref"]), (what, stats)
+    return stats

@@ -96,3 +96,14 @@ def test_oracle_top_p_inverse_cdf_edges():
     assert R.top_p_with_uniforms(logits, 1.0, 0.0, torch.tensor([0.9])).item() == 0
     # temperature 0 is greedy
     assert R.top_p_with_uniforms(logits, 0.0, 0.5, torch.tensor([0.9])).item() == 0
+
+
+def test_oracle_exposes_the_parity_helpers_the_gpu_tests_use():
+    """The GPU tests and smoke() call these; a missing one would only show on a GPU."""
+    from oracle import stage_ref as R
+
+    for name in ("exact_bar", "exact_rounding", "top_p_acceptable", "top_p_with_uniforms", "top_p_nucleus",
+                 "build_stages", "prefill", "decode_step", "greedy"):
+        assert callable(getattr(R, name)), name
+    z = torch.zeros(4)
+    assert R.exact_bar(z, z, z)["max_got"] == 0.0
