@@ -47,15 +47,8 @@ using bf16 = __nv_bfloat16;
 constexpr int kRowsT = 128;              // query rows of a tile = TMEM lanes
 constexpr int kChunkT = kKvBoxKeys;      // keys per chunk (128)
 constexpr int kBoxT = kKvBoxKeys * 128;  // a 128-row x 128-byte swizzled block (16 KB)
-// Softmax threads per query row: head_dim 128 splits a row's keys and dims
-// four ways (16 softmax warps: more warps to hide the TMEM and exponential
-// latencies of each other), head_dim 64 two ways (8 warps).
-template <int D>
-struct SoftSplit {
-  static constexpr int kParts = D == 128 ? 4 : 2;
-  static constexpr int kWarps = 4 * kParts;  // one per TMEM lane quadrant and part
-  static constexpr int kThreads = 64 + 32 * kWarps;
-};
+constexpr int kSoftWarps = 8;            // two per TMEM lane quadrant, 64 keys each
+constexpr int kThreadsT = 64 + 32 * kSoftWarps;
 constexpr int kColS = 0;                 // TMEM columns: scores [0, 256) in two buffers,
 constexpr int kColO = 256;               // the output [256, 256 + D)
 
@@ -68,8 +61,8 @@ struct TcPrefillLayout {
   static constexpr int kOffQ = 0;
   static constexpr int kOffKV = kOffQ + kQ;
   static constexpr int kOffBar = kOffKV + kStages * 2 * kKV;
-  static constexpr int kOffX = kOffBar + 128;          // [2 chunk parities][parts][128 rows] floats
-  static constexpr int kBytes = kOffX + 2 * SoftSplit<D>::kParts * 128 * 4 + 1024;
+  static constexpr int kOffX = kOffBar + 128;          // [2 chunk parities][2 halves][128 rows] floats
+  static constexpr int kBytes = kOffX + 2048 + 1024;
 };
 
 // Shared-memory descriptor of an MN-major operand with 128-byte swizzle: 64
@@ -116,7 +109,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 template <int D>
-__global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_kernel(AttnArgs a, PrefillPlan pl) {
+__global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs a, PrefillPlan pl) {
   using L = TcPrefillLayout<D>;
   constexpr int DB = L::kDB;
   const int G = a.nq / a.nkv;
@@ -134,9 +127,7 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
   uint64_t* drain = bars + 9;    // every MMA finished
   uint32_t* tmem_holder = (uint32_t*)(bars + 10);
   volatile int* abort_flag = (volatile int*)(tmem_holder + 1);
-  float* xch = (float*)(smem + L::kOffX);  // a row's partial maxima (then sums) of its parts
-  constexpr int kParts = SoftSplit<D>::kParts;
-  constexpr int kSoftWarps = SoftSplit<D>::kWarps;
+  float* xch = (float*)(smem + L::kOffX);  // a row's partial maxima (then sums) of the two halves
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -265,30 +256,28 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
       mma_commit(drain);  // arrives once every MMA issued above has finished
     }
   } else {
-    // Softmax warps: warp w owns TMEM lanes 32·(w % 4) .. + 31 (one query row
-    // per thread) and part (w - 2) / 4 of every chunk's keys (and of the head
-    // dims for the query, output and rescale); the kParts warps of a lane
-    // quadrant form a row group.
+    // Softmax warps 2-9: warp w owns TMEM lanes 32·(w % 4) .. + 31 (one query
+    // row per thread) and half (w - 2) / 4 of every chunk's keys (and of the
+    // head dims for the query, output and rescale).
     const int q4 = warp & 3;
-    const int part = (warp - 2) >> 2;
+    const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
     const float scale2 = a.scale * 1.4426950408889634f;
-    constexpr int kHK = kChunkT / kParts;  // keys of this part
-    constexpr int kHD = D / kParts;        // dims of this part
-    constexpr int kGroup = 32 * kParts;    // threads of a row group
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + q4), "n"(kGroup) : "memory"); };
-    // The warps of a row group decide together whether a wait failed, so
-    // none is left at a group barrier another has abandoned.
+    constexpr int kHK = kChunkT / 2;  // keys of this half
+    constexpr int kHD = D / 2;        // dims of this half
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + q4) : "memory"); };
+    // The two warps of a row pair decide together whether a wait failed, so
+    // neither is left at a pair barrier the other has abandoned.
     auto pair_any = [&](bool pred) -> bool {
       uint32_t res;
       asm volatile(
           "{\n\t.reg .pred p, q;\n\t"
           "setp.ne.u32 p, %1, 0;\n\t"
-          "barrier.red.or.pred q, %2, %3, p;\n\t"
+          "barrier.red.or.pred q, %2, 64, p;\n\t"
           "selp.u32 %0, 1, 0, q;\n\t}"
           : "=r"(res)
-          : "r"((uint32_t)pred), "r"(1 + q4), "n"(kGroup)
+          : "r"((uint32_t)pred), "r"(1 + q4)
           : "memory");
       return res != 0;
     };
@@ -313,12 +302,12 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
       const bool valid = r / G < pl.tq && s_tok < a.S;
       const int vis = valid ? visible(a, rd, b * a.S + s_tok, s_tok) : 0;
       const int tot = rd.past + a.S;  // keys written so far
-      // This part of the query row into the tile (zeros for rows past the sequence).
+      // This half of the query row into the tile (zeros for rows past the sequence).
       {
         const uint4* src = reinterpret_cast<const uint4*>(
             (const bf16*)a.q + (((size_t)b * a.S + (valid ? s_tok : 0)) * a.nq + (size_t)h * G + g) * D);
 #pragma unroll
-        for (int c = part * (kHD / 8); c < (part + 1) * (kHD / 8); ++c) {
+        for (int c = half * (kHD / 8); c < (half + 1) * (kHD / 8); ++c) {
           const uint4 val = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
           *reinterpret_cast<uint4*>(sq + swz_off(r, c)) = val;
         }
@@ -327,7 +316,7 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
       __syncwarp();
       if (lane == 0) mbar_arrive(qready);
 
-      float m = -INFINITY, l = 0.f;  // m: the running maximum P is taken against (raw scores); l: this part's sum
+      float m = -INFINITY, l = 0.f;  // m: the running maximum P is taken against (raw scores); l: this half's sum
       for (int ch = 0; ch < nch; ++ch, ++n) {
         const int sb = (int)(n & 1);
         // scores ready; the chunk's load is complete too (it orders the TMA
@@ -342,8 +331,8 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
         float sc[kHK];
 #pragma unroll
         for (int c4 = 0; c4 < kHK / 32; ++c4)
-          tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + part * kHK + c4 * 32, sc + c4 * 32);
-        const int nv = vis - ch * kChunkT - part * kHK;  // visible keys of this part for this row
+          tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * kHK + c4 * 32, sc + c4 * 32);
+        const int nv = vis - ch * kChunkT - half * kHK;  // visible keys of this half for this row
         // Row maximum of the raw scores (the scale is positive, so it commutes
         // with the maximum), as a tree; invisible keys become -inf.
         if (!__all_sync(0xffffffffu, nv >= kHK)) {
@@ -357,12 +346,10 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
         for (int c = 8; c < kHK; ++c) t8[c & 7] = fmaxf(t8[c & 7], sc[c]);
         const float pm = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
                                fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
-        float* xs = xch + (size_t)(sb * kParts) * kRowsT;
-        xs[part * kRowsT + r] = pm;
+        float* xs = xch + (size_t)(sb * 2) * kRowsT;
+        xs[half * kRowsT + r] = pm;
         pair_sync();  // (double-buffered by chunk parity: one barrier per chunk)
-        float mt = xs[r];
-#pragma unroll
-        for (int j = 1; j < kParts; ++j) mt = fmaxf(mt, xs[j * kRowsT + r]);
+        const float mt = fmaxf(pm, xs[(1 - half) * kRowsT + r]);
         // Move the maximum only when the scores outgrow it by 2^8.
         float m_new = m;
         bool moved = false;
@@ -388,10 +375,10 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
 #pragma unroll 1
           for (int c4 = 0; c4 < kHD / 32; ++c4) {
             float o[32];
-            tmem_ld32(tmem + lanes + kColO + part * kHD + c4 * 32, o);
+            tmem_ld32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(tmem + lanes + kColO + part * kHD + c4 * 32, o);
+            tmem_st32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
           }
         }
         // P = 2^(S·scale2 - m·scale2): one fused multiply-add and one ex2 per
@@ -406,27 +393,26 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
         }
         l = l * alpha + (((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7])));
         m = m_new;
-        // Value rows past the written keys: clear this part of them before the product.
+        // Value rows past the written keys: clear this half of them before the product.
         if (ch * kChunkT + kChunkT > tot && ch * kChunkT + r >= tot) {
           uint8_t* v = skv + sb * 2 * L::kKV + L::kKV;
 #pragma unroll
-          for (int c = part * (kHD / 8); c < (part + 1) * (kHD / 8); ++c)
+          for (int c = half * (kHD / 8); c < (half + 1) * (kHD / 8); ++c)
             *reinterpret_cast<uint4*>(v + (c >> 3) * kBoxT + r * 128 + (c & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
         // P as bf16 high + low parts into the chunk's score buffer (its scores
-        // are in registers in every part: the group barrier above): high at
-        // columns [kPC·part, +kPC), low 64 columns on.
+        // are in registers on both halves: the pair barrier above): high at
+        // columns [32·half, +32), low 64 columns on.
         {
-          constexpr int kPC = kHK / 2;  // packed key pairs of this part
-          float hw[kPC], lw[kPC];
+          float hw[32], lw[32];
 #pragma unroll
-          for (int j = 0; j < kPC; ++j) {
+          for (int j = 0; j < 32; ++j) {
             const uint32_t hv = cvt_bf16x2(sc[2 * j], sc[2 * j + 1]);
             hw[j] = __uint_as_float(hv);
             lw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j] - lo_bf16(hv), sc[2 * j + 1] - hi_bf16(hv)));
           }
-          tmem_st_n<kPC>(tmem + lanes + kColS + (uint32_t)sb * kChunkT + part * kPC, hw);
-          tmem_st_n<kPC>(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + part * kPC, lw);
+          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, hw);
+          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + half * 32, lw);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -434,17 +420,14 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
         if (lane == 0) mbar_arrive(pready);
       }
       if (!ok) break;
-      // The row sum of the parts (in part order, so every part holds the
-      // same sum), then O / l for this part of the dims.
+      // The row sum from both halves, then O / l for this half of the dims.
       {
-        float* xs = xch + (size_t)((n & 1) * kParts) * kRowsT;
-        xs[part * kRowsT + r] = l;
+        float* xs = xch + (size_t)((n & 1) * 2) * kRowsT;
+        xs[half * kRowsT + r] = l;
         pair_sync();
-        float tot_l = xs[r];
-#pragma unroll
-        for (int j = 1; j < kParts; ++j) tot_l += xs[j * kRowsT + r];
+        const float lo = xs[(1 - half) * kRowsT + r];
         pair_sync();  // read before the next item's chunk of the same parity writes
-        l = tot_l;
+        l += lo;
       }
       if (nch > 0) {
         if (pair_any(!wait_odone(n - 1))) {
@@ -460,7 +443,7 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
       for (int c4 = 0; c4 < kHD / 32; ++c4) {
         float o[32];
         if (nch > 0) {
-          tmem_ld32(tmem + lanes + kColO + part * kHD + c4 * 32, o);
+          tmem_ld32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0.f;
@@ -473,7 +456,7 @@ __global__ void __launch_bounds__(SoftSplit<D>::kThreads, 1) attn_prefill_tc_ker
             w.y = pack2(o[8 * e8 + 2] * inv, o[8 * e8 + 3] * inv);
             w.z = pack2(o[8 * e8 + 4] * inv, o[8 * e8 + 5] * inv);
             w.w = pack2(o[8 * e8 + 6] * inv, o[8 * e8 + 7] * inv);
-            *reinterpret_cast<uint4*>(out + part * kHD + c4 * 32 + 8 * e8) = w;
+            *reinterpret_cast<uint4*>(out + half * kHD + c4 * 32 + 8 * e8) = w;
           }
         }
       }
@@ -515,7 +498,7 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s) {
   pl.ntiles = (a.S + pl.tq - 1) / pl.tq;
   pl.items = (long long)pl.ntiles * a.B * a.nkv;
   if (pl.items <= 0) return cudaSuccess;
-  auto go = [&](auto kernel, int smem, int threads) -> cudaError_t {
+  auto go = [&](auto kernel, int smem) -> cudaError_t {
     static bool configured[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -528,10 +511,10 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s) {
     }
     const long long cap = sm_count_prefill_tc();
     const int grid = (int)(pl.items < cap ? pl.items : cap);
-    return launch_pdl(kernel, dim3(grid), dim3(threads), smem, s, a, pl);
+    return launch_pdl(kernel, dim3(grid), dim3(kThreadsT), smem, s, a, pl);
   };
-  if (a.D == 128) return go(attn_prefill_tc_kernel<128>, TcPrefillLayout<128>::kBytes, SoftSplit<128>::kThreads);
-  return go(attn_prefill_tc_kernel<64>, TcPrefillLayout<64>::kBytes, SoftSplit<64>::kThreads);
+  if (a.D == 128) return go(attn_prefill_tc_kernel<128>, TcPrefillLayout<128>::kBytes);
+  return go(attn_prefill_tc_kernel<64>, TcPrefillLayout<64>::kBytes);
 }
 
 }  // namespace mg

@@ -164,28 +164,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Store 16 consecutive columns of this warp's 32 TMEM lanes and wait for the store.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-  uint32_t r[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-// tmem_st16 or tmem_st32 by column count.
-template <int N>
-__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const float* v) {
-  static_assert(N == 16 || N == 32, "16 or 32 columns");
-  if constexpr (N == 32) tmem_st32(taddr, v);
-  else tmem_st16(taddr, v);
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
   const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
