@@ -329,9 +329,13 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         float sc[kHK];
+        if constexpr (D == 128) {  // one 64-column load and one wait (head_dim 64 would spill)
+          tmem_ld64(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * kHK, sc);
+        } else {
 #pragma unroll
-        for (int c4 = 0; c4 < kHK / 32; ++c4)
-          tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * kHK + c4 * 32, sc + c4 * 32);
+          for (int c4 = 0; c4 < kHK / 32; ++c4)
+            tmem_ld32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * kHK + c4 * 32, sc + c4 * 32);
+        }
         const int nv = vis - ch * kChunkT - half * kHK;  // visible keys of this half for this row
         // Row maximum of the raw scores (the scale is positive, so it commutes
         // with the maximum), as a tree; invisible keys become -inf.
@@ -411,8 +415,9 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
             hw[j] = __uint_as_float(hv);
             lw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j] - lo_bf16(hv), sc[2 * j + 1] - hi_bf16(hv)));
           }
-          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, hw);
-          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + half * 32, lw);
+          tmem_st32_nowait(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, hw);
+          tmem_st32_nowait(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + half * 32, lw);
+          tmem_wait_st();
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
