@@ -140,9 +140,6 @@ struct mg_stage {
   size_t work_scratch = 0;
   int* counters = nullptr;  // stream-K tile counters: zero between launches
   size_t counters_elems = 0;
-  int* chain_bar = nullptr;  // layer-chain grid barrier: arrivals so far (wrapping)
-  int chain_gen = 0;         // the value the device word holds between launches
-  bool chain_enabled = false; // MESHGPU_LAYER_CHAIN=1 turns the decode layer chain on
   // Greedy selection fused into lm_head (Greedy): zero between launches.
   unsigned long long* greedy_best = nullptr;
   int* greedy_done = nullptr;
@@ -233,7 +230,6 @@ size_t scratch_needed(const mg_stage* st, int M, int rows, int max_keys) {
   }
   s = std::max(s, attention_scratch_elems(M, st->nq, st->D, max_keys));
   if (M <= 32) {
-    s = std::max(s, layer_chain_scratch_elems());
     s = std::max(s, linear_scratch_elems(dt, M, st->Nqkv, st->H, kEpiPieces));
     s = std::max(s, linear_scratch_elems(dt, M, st->H, st->nq * st->D, kEpiPieces));
     s = std::max(s, linear_scratch_elems(dt, M, st->H, st->I, kEpiPieces));
@@ -270,7 +266,6 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   if (st->cfg.has_lm_head) n_counters = std::max(n_counters, gemv_tc_tiles(st->V, kEpiStore));
   n_counters = std::max(n_counters, (size_t)Mt * st->nkv);  // attention: one per (token, KV head)
   const size_t o_counters = take(n_counters * sizeof(int));
-  const size_t o_bar = take(64 * sizeof(int));  // two words, 128 bytes apart
   const size_t o_greedy = take(64 * sizeof(unsigned long long));  // best[32], done
   if (st->work) {
     MG_CUDA(cudaDeviceSynchronize(), "synchronize before work resize");
@@ -297,9 +292,6 @@ int ensure_work(mg_stage* st, int M, int rows, int max_keys) {
   st->counters = (int*)(base + o_counters);
   st->counters_elems = n_counters;
   MG_CUDA(cudaMemset(st->counters, 0, n_counters * sizeof(int)), "zero tile counters");
-  st->chain_bar = (int*)(base + o_bar);
-  st->chain_gen = 0;
-  MG_CUDA(cudaMemset(st->chain_bar, 0, 64 * sizeof(int)), "zero chain barrier");
   st->greedy_best = (unsigned long long*)(base + o_greedy);
   st->greedy_done = (int*)(st->greedy_best + 32);
   MG_CUDA(cudaMemset(st->greedy_best, 0, 64 * sizeof(unsigned long long)), "zero greedy selection");
@@ -547,16 +539,12 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
       attn_flops += 4.0 * vis * qd;
     }
   }
-  // Decode batches (<= 32 token rows) run everything between two attention
-  // launches as one layer-chain launch; the rest runs kernel by kernel.
   const bool last_only = out_mode == MG_OUT_LOGITS_LAST;
   const int rows_out = last_only ? B : M;
-  const bool fuse_greedy = greedy_ids && c.has_lm_head && !st->chain_enabled &&
-                           gemv_tc_applicable(dt, rows_out, st->V, H);
+  const bool fuse_greedy = greedy_ids && c.has_lm_head && gemv_tc_applicable(dt, rows_out, st->V, H);
   // Top-p rows: the lm_head's epilogue counts the bf16 logits by value
   // (kEpiHist) and one selection kernel draws from the histograms.
-  const bool fuse_hist = tp && c.has_lm_head && !st->chain_enabled && dt == kBF16 &&
-                         gemv_tc_applicable(dt, rows_out, st->V, H);
+  const bool fuse_hist = tp && c.has_lm_head && dt == kBF16 && gemv_tc_applicable(dt, rows_out, st->V, H);
   int* hist = nullptr;
   if (tp && dt == kBF16) {
     hist = top_p_hist_buffer(rows_out);
@@ -577,101 +565,8 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
     }
     out = st->greedy_logits;
   }
-  ChainArgs ca{};
-  ca.dtype = dt;
-  ca.M = M;
-  ca.partial = st->part;
-  ca.partial_elems = st->work_scratch;
-  ca.counters = st->counters;
-  ca.counters_elems = st->counters_elems;
-  ca.err = st->err;
-  ca.bar = st->chain_bar;
-  bool lm_in_chain = false;
   bool final_norm_done = false;  // the last residual kernel also ran the final norm
-  auto chain_linear = [&](ChainStep& cs, const void* X, int64_t ldx, const void* W, void* Y, int64_t ldy,
-                          const void* R, int64_t ldr, int N, int K, int epi) {
-    cs.kind = kChainLinear;
-    cs.X = X; cs.ldx = ldx; cs.W = W; cs.Y = Y; cs.ldy = ldy; cs.R = R; cs.ldr = ldr;
-    cs.N = N; cs.K = K; cs.epilogue = epi;
-  };
-  auto chain_norm = [&](ChainStep& cs, const void* x, int64_t xs, const void* w) {
-    cs.kind = kChainNorm;
-    cs.x = x; cs.xs = xs; cs.w = w; cs.y = st->xn; cs.H = H; cs.eps = c.rms_norm_eps;
-  };
-  // Steps after layer l's attention: o_proj, post-attention norm, gate/up,
-  // down, then the next layer's input norm and qkv (or final norm, lm_head).
-  auto build_chain = [&](int l) {
-    const LayerW& w = st->layers[l];
-    int n = 0;
-    chain_linear(ca.step[n++], st->attn, qd, w.wo, st->x, H, st->x, H, H, qd, kEpiResid);
-    chain_norm(ca.step[n++], st->x, H, w.ln2);
-    chain_linear(ca.step[n++], st->xn, H, w.wgu, st->h, st->I, nullptr, 0, st->I, H, kEpiSwiGLU);
-    chain_linear(ca.step[n++], st->h, st->I, w.wd, st->x, H, st->x, H, H, st->I, kEpiResid);
-    lm_in_chain = false;
-    if (l + 1 < st->L) {
-      const LayerW& wn = st->layers[l + 1];
-      chain_norm(ca.step[n++], st->x, H, wn.ln1);
-      chain_linear(ca.step[n++], st->xn, H, wn.wqkv, st->qkv, st->Nqkv, nullptr, 0, st->Nqkv, H, kEpiStore);
-    } else if (c.has_lm_head && rows_out == M) {
-      chain_norm(ca.step[n++], st->x, H, st->norm);
-      chain_linear(ca.step[n++], st->xn, H, st->lm_head, out, st->V, nullptr, 0, st->V, H, kEpiStore);
-      lm_in_chain = true;
-    }
-    ca.nsteps = n;
-  };
-  bool use_chain = st->chain_enabled && M <= 32 && st->L > 0;
-  if (use_chain) {
-    build_chain(st->L - 1);  // the longest chain (lm_head) decides
-    use_chain = layer_chain_applicable(ca);
-    if (use_chain && st->L > 1) {
-      build_chain(0);
-      use_chain = layer_chain_applicable(ca);
-    }
-    lm_in_chain = false;  // set again by the real last-layer chain
-  }
-  auto chain_bytes = [&]() {
-    double b = 0;
-    for (int j = 0; j < ca.nsteps; ++j) {
-      const ChainStep& cs = ca.step[j];
-      if (cs.kind == kChainNorm) {
-        b += 2.0 * M * H * st->esz;
-      } else {
-        const double wrows = cs.epilogue == kEpiSwiGLU ? 2.0 * cs.N : (double)cs.N;
-        b += (wrows * cs.K + (double)M * cs.K + (double)M * cs.N * (cs.epilogue == kEpiResid ? 2 : 1)) * st->esz;
-      }
-    }
-    return b;
-  };
-  auto chain_flops = [&]() {
-    double f = 0;
-    for (int j = 0; j < ca.nsteps; ++j) {
-      const ChainStep& cs = ca.step[j];
-      if (cs.kind == kChainLinear) f += 2.0 * M * (cs.epilogue == kEpiSwiGLU ? 2.0 * cs.N : (double)cs.N) * cs.K;
-    }
-    return f;
-  };
-
-  if (use_chain) {
-    const LayerW& w0 = st->layers[0];
-    MG_TIMED(MG_PROF_OTHER, norm_bytes, 0, launch_rmsnorm(dt, st->x, H, w0.ln1, M, H, c.rms_norm_eps, st->xn, s), "input_layernorm");
-    la.X = st->xn; la.ldx = H; la.W = w0.wqkv; la.Y = st->qkv; la.ldy = st->Nqkv;
-    la.N = st->Nqkv; la.K = H; la.epilogue = kEpiStore; la.R = nullptr;
-    MG_TIMED(linear_class(la), linear_bytes(la, st->esz), linear_flops(la), launch_linear(la, s), "qkv projection");
-    for (int l = 0; l < st->L; ++l) {
-      const LayerW& w = st->layers[l];
-      qa.layer = l;
-      qa.q_norm = w.qn;
-      qa.k_norm = w.kn;
-      MG_TIMED(MG_PROF_OTHER, 2.0 * M * st->Nqkv * st->esz, 0, launch_qkv_post(qa, s), "rope / kv append");
-      aa.layer = l;
-      MG_TIMED(MG_PROF_ATTENTION, attn_bytes, attn_flops, launch_attention(aa, s), "attention");
-      build_chain(l);
-      ca.bar_base = st->chain_gen;
-      MG_TIMED(MG_PROF_LINEAR_DECODE, chain_bytes(), chain_flops(), launch_layer_chain(ca, s), "layer chain");
-      st->chain_gen = (int)((unsigned)st->chain_gen +
-                            (unsigned)(ca.nsteps - 1) * (unsigned)layer_chain_grid());  // wraps like the device word
-    }
-  } else {
+  {
     // Decode rows on the tcgen05 GEMM: the qkv, o_proj and down projections
     // leave their fp32 pieces, and the kernel after each (RoPE / append, or
     // the residual add + RMSNorm) adds them, so no GEMM ends in a fix-up.
@@ -732,9 +627,7 @@ int run_stage(mg_stage* st, const std::vector<RowDesc>& rows, int S, const int64
     }
   }
 
-  if (lm_in_chain) {
-    // final norm and lm_head ran as the last layer chain's steps
-  } else if (c.has_lm_head) {
+  if (c.has_lm_head) {
     const void* src = last_only ? (const void*)((const char*)st->x + (size_t)(S - 1) * H * st->esz)
                                 : st->x;
     const int64_t stride = last_only ? (int64_t)S * H : H;
@@ -821,7 +714,6 @@ int mg_stage_create(const mg_stage_config* cfg, const mg_stage_weights* w, mg_st
 
   DeviceGuard guard(c.device);
   mg_stage* st = new mg_stage();
-  if (const char* env = getenv("MESHGPU_LAYER_CHAIN")) st->chain_enabled = strcmp(env, "1") == 0;
   st->cfg = c;
   st->L = c.layer_end - c.layer_start;
   st->nq = c.num_attention_heads;
@@ -1216,8 +1108,6 @@ int mg_stage_check_device(mg_stage* st, void* stream) {
     // A tensor-core kernel gave up waiting for its data; its tile counters
     // may be left mid-count, so clear them before the next forward.
     if (st->counters) cudaMemset(st->counters, 0, st->counters_elems * sizeof(int));
-    if (st->chain_bar) cudaMemset(st->chain_bar, 0, 64 * sizeof(int));
-    st->chain_gen = 0;
     if (st->greedy_best) cudaMemset(st->greedy_best, 0, 64 * sizeof(unsigned long long));
     return fail(MG_ETIMEOUT, "a kernel gave up a bounded wait (code 3); the outputs of the "
                              "forwards since the last check are invalid");

@@ -34,10 +34,10 @@ __global__ void embed_kernel(const T* __restrict__ table, const int64_t* __restr
   for (int i = threadIdx.x; i < H / VEC; i += blockDim.x) dst[i] = src[i];
 }
 
-// RMSNorm reduction order, shared by every kernel that normalises a row
-// (this file and the layer chain): 512 threads, thread j adds the squares of
-// the 16-byte vectors j, j + 512, ... (each vector's elements in order), then
-// a butterfly over each warp's 32 lanes, then over the 16 warp sums.
+// RMSNorm reduction order, shared by every kernel that normalises a row: 512
+// threads, thread j adds the squares of the 16-byte vectors j, j + 512, ...
+// (each vector's elements in order), then a butterfly over each warp's 32
+// lanes, then over the 16 warp sums.
 template <typename T>
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);

@@ -349,9 +349,9 @@ uint64_t mg_launch_count(void);
 int mg_peer_access(int32_t device, int32_t peer, int32_t* enabled);
 
 /* Leave `n` SMs of `device` (0 <= n <= half of them) out of the persistent
- * decode kernels' grids (the decode GEMM, decode and prefill attention, the
- * layer chain), so kernels that run beside them (NCCL's send/receive
- * kernels in a multi-process pipeline) never hold back one of their CTAs.
+ * decode kernels' grids (the decode GEMM, decode and prefill attention), so
+ * kernels that run beside them (NCCL's send/receive kernels in a
+ * multi-process pipeline) never hold back one of their CTAs.
  * Set it before the stage runs; 0 by default. */
 int mg_reserve_sms(int32_t device, int32_t n);
 
