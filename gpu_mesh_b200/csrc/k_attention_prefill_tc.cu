@@ -23,9 +23,11 @@
 //     softmax in base 2 (P = 2^(S·scale2 - m·scale2), l = l·α + ΣP).  The
 //     running maximum m is moved only when a row's scores exceed it by more
 //     than 2^8, and only then is the row of O in TMEM rescaled by α (the
-//     result O / l does not depend on which m is used).  P goes back into
-//     TMEM as bf16 high + low parts (two MMAs, so the weights keep fp32
-//     accuracy).  At the end they write O / l.
+//     result O / l does not depend on which m is used).  The exponentials
+//     of chunk j are computed while the value product of chunk j - 1 runs;
+//     P goes back into TMEM as bf16 (the precision the reference's own
+//     attention multiplies the values in), l sums it in fp32.  At the end
+//     they write O / l.
 // Value rows at or past the cache end were never written: they are cleared
 // in shared memory before the value product (P is 0 there, but 0 * NaN is
 // not).  Every wait is bounded (code 3 in the error word on expiry); on
@@ -208,14 +210,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         if (!mbar_wait(pready, (int)(m & 1), a.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint8_t* v = skv + (int)(m & 1) * 2 * L::kKV + L::kKV;
-        const uint32_t pt = tmem + kColS + (uint32_t)(m & 1) * kChunkT;  // P high, then P low 64 columns on
+        const uint32_t pt = tmem + kColS + (uint32_t)(m & 1) * kChunkT;  // P: 128 keys in 64 columns
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {
-#pragma unroll
-          for (int kk = 0; kk < kChunkT / 16; ++kk)
-            mma_bf16_ta(tmem + kColO, pt + part * (kChunkT / 2) + kk * 8, smem_desc_mn(v + kk * 16 * 128, kBoxT),
-                        idPV, (first && part == 0 && kk == 0) ? 0u : 1u);
-        }
+        for (int kk = 0; kk < kChunkT / 16; ++kk)
+          mma_bf16_ta(tmem + kColO, pt + kk * 8, smem_desc_mn(v + kk * 16 * 128, kBoxT), idPV,
+                      (first && kk == 0) ? 0u : 1u);
         mma_commit(odone);
         mma_commit(&kvempty[m & 1]);
         return true;
@@ -364,11 +363,24 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
           moved = true;
         }
         const float alpha = moved ? ex2_approx((m - m_new) * scale2) : 1.f;
-        // The previous value product is done before this chunk's P goes into
-        // TMEM and before O is rescaled.  Waiting for it here (not for the
-        // one before) also keeps this thread's odone waits within one phase
-        // of the barrier: value product n can only start after this chunk's
-        // P is handed over.
+        // P = 2^(S·scale2 - m·scale2): one fused multiply-add and one ex2 per
+        // key (invisible keys are -inf and give 0).  This runs while the
+        // previous chunk's value product is still on the tensor cores.
+        const float mb = m_new == -INFINITY ? 0.f : m_new * scale2;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t8[j] = 0.f;
+#pragma unroll
+        for (int c = 0; c < kHK; ++c) {
+          sc[c] = ex2_approx(fmaf(sc[c], scale2, -mb));
+          t8[c & 7] += sc[c];
+        }
+        l = l * alpha + (((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7])));
+        m = m_new;
+        // The previous value product is done before O is rescaled and this
+        // chunk's P is handed over.  Waiting for it on every chunk (not for
+        // the one before) also keeps this thread's odone waits within one
+        // phase of the barrier: value product n can only start after this
+        // chunk's P is handed over.
         const bool rescale = __any_sync(0xffffffffu, moved);
         if (pair_any(!wait_odone(n - 1))) {
           ok = false;
@@ -385,18 +397,6 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
             tmem_st32(tmem + lanes + kColO + half * kHD + c4 * 32, o);
           }
         }
-        // P = 2^(S·scale2 - m·scale2): one fused multiply-add and one ex2 per
-        // key (invisible keys are -inf and give 0).
-        const float mb = m_new == -INFINITY ? 0.f : m_new * scale2;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) t8[j] = 0.f;
-#pragma unroll
-        for (int c = 0; c < kHK; ++c) {
-          sc[c] = ex2_approx(fmaf(sc[c], scale2, -mb));
-          t8[c & 7] += sc[c];
-        }
-        l = l * alpha + (((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7])));
-        m = m_new;
         // Value rows past the written keys: clear this half of them before the product.
         if (ch * kChunkT + kChunkT > tot && ch * kChunkT + r >= tot) {
           uint8_t* v = skv + sb * 2 * L::kKV + L::kKV;
@@ -404,20 +404,14 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
           for (int c = half * (kHD / 8); c < (half + 1) * (kHD / 8); ++c)
             *reinterpret_cast<uint4*>(v + (c >> 3) * kBoxT + r * 128 + (c & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
-        // P as bf16 high + low parts into the chunk's score buffer (its scores
-        // are in registers on both halves: the pair barrier above): high at
-        // columns [32·half, +32), low 64 columns on.
+        // P as bf16 into the chunk's score buffer (its scores are in
+        // registers on both halves: the pair barrier above), two keys per
+        // column, this half's keys at columns [32·half, +32).
         {
-          float hw[32], lw[32];
+          float pw[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint32_t hv = cvt_bf16x2(sc[2 * j], sc[2 * j + 1]);
-            hw[j] = __uint_as_float(hv);
-            lw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j] - lo_bf16(hv), sc[2 * j + 1] - hi_bf16(hv)));
-          }
-          tmem_st32_nowait(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, hw);
-          tmem_st32_nowait(tmem + lanes + kColS + (uint32_t)sb * kChunkT + kChunkT / 2 + half * 32, lw);
-          tmem_wait_st();
+          for (int j = 0; j < 32; ++j) pw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j], sc[2 * j + 1]));
+          tmem_st32(tmem + lanes + kColS + (uint32_t)sb * kChunkT + half * 32, pw);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
