@@ -396,10 +396,13 @@ __global__ void __launch_bounds__(kSelThreads) top_p_select_kernel(
   int dmax = INT_MAX;
   for (int i = 0; i < kSelWarps; ++i) dmax = min(dmax, wfirst[i]);
   const float ms = dmax == INT_MAX ? 0.f : hist_value((uint32_t)(kHistBins - 1 - dmax)) / temperature;
+  // A slab without tokens adds exactly +0 to every sum and scan below, so
+  // it is skipped (most of the 65536 values are absent from a row).
   float acc = 0.f;
   for (int k = 0; k < kSlabs; ++k) {
     const uint32_t b = bin_at(k);
     const int c = count_at(b);
+    if (!__ballot_sync(0xffffffffu, c > 0)) continue;
     acc += warp_sum(c > 0 ? (float)c * expf(hist_value(b) / temperature - ms) : 0.f);
   }
   if (lane == 0) wsum[warp] = acc;
@@ -414,18 +417,21 @@ __global__ void __launch_bounds__(kSelThreads) top_p_select_kernel(
   for (int k = 0; k < kSlabs; ++k) {
     const uint32_t b = bin_at(k);
     const int c = count_at(b);
+    if (!__ballot_sync(0xffffffffu, c > 0)) continue;
     acc += warp_sum(c > 0 ? (float)c * prob(b) : 0.f);
   }
   if (lane == 0) wsum[warp] = acc;
   __syncthreads();
   float above = 0.f;  // mass of the bins before this warp's range
   for (int i = 0; i < warp; ++i) above += wsum[i];
-  // Walk this warp's slabs; `visit(k, gt, c, p, kept)` sees each bin.
+  // Walk this warp's slabs; `visit(k, gt, c, p, kept)` sees each bin of every
+  // slab that holds a token.
   auto walk = [&](auto&& visit) {
     float carry = above;
     for (int k = 0; k < kSlabs; ++k) {
       const uint32_t b = bin_at(k);
       const int c = count_at(b);
+      if (!__ballot_sync(0xffffffffu, c > 0)) continue;  // nothing kept, no mass: the carry stands
       const float p = c > 0 ? prob(b) : 0.f;
       const float mass = (float)c * p;
       const float incl = warp_incl_scan(mass, lane);
