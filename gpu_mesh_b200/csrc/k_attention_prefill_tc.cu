@@ -334,8 +334,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         float sc[kChunkT];
-        tmem_ld64(tmem + lanes + kColS + 128 * x, sc);
-        tmem_ld64(tmem + lanes + kColS + 128 * x + 64, sc + 64);
+        tmem_ld128(tmem + lanes + kColS + 128 * x, sc);
         const int nv = vis - ch * kChunkT;  // visible keys of this chunk for this row
         if (!__all_sync(0xffffffffu, nv >= kChunkT)) {
 #pragma unroll
@@ -373,13 +372,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         l = l * alpha + (((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7])));
         m = m_new;
         // P as bf16 over the chunk's scores, two keys per column.
+        {
+          float pw[kChunkT / 2];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float pw[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            pw[j] = __uint_as_float(cvt_bf16x2(sc[64 * half + 2 * j], sc[64 * half + 2 * j + 1]));
-          tmem_st32(tmem + lanes + kColS + 128 * x + 32 * half, pw);
+          for (int j = 0; j < kChunkT / 2; ++j) pw[j] = __uint_as_float(cvt_bf16x2(sc[2 * j], sc[2 * j + 1]));
+          tmem_st64(tmem + lanes + kColS + 128 * x, pw);
         }
         // The previous value product of this tile has finished (the score
         // product just read was issued after it): rescale O's row in TMEM
