@@ -6,9 +6,13 @@
 // tiles of the same (b, h), A (earlier tokens) and B, which share every key
 // and value chunk they both see.  The kernel is persistent (one CTA per SM,
 // items heaviest first) and splits the flash recurrence over its warps:
-//   * warp 0, one lane: loads each 128-key chunk of keys and values with 2-D
-//     TMA through the slot's tensor map (box 128 keys x 64 dims, 128-byte
-//     swizzle, no multicast) into a 2-stage ring;
+//   * warp 0, one lane: loads both tiles' query rows with 4-D TMA over the
+//     query buffer {D, heads, tokens, rows} (box 64 dims x G heads x 128 / G
+//     tokens, tokens past the sequence read as zeros), the next item's as soon
+//     as the current item's last score product of the tile is done; and each
+//     128-key chunk of keys and values with 2-D TMA through the slot's tensor
+//     map (box 128 keys x 64 dims, 128-byte swizzle, no multicast) into a
+//     2-stage ring;
 //   * warp 1, one lane: issues tcgen05.mma.  For tile X: S_X = Q_X·Kᵀ (M =
 //     128 query rows, N = 128 keys, K = D) into X's TMEM score columns, and
 //     O_X += P_X·V (M = 128 rows, N = D, K = 128 keys) into X's TMEM output,
@@ -18,10 +22,9 @@
 //     its score product of chunk j + 1 run while B's softmax works on chunk
 //     j, and the other way round;
 //   * warps 2-5 (tile A) and 6-9 (tile B): one thread per query row (its
-//     TMEM lane).  They write their tile's query rows into shared memory, and
-//     per chunk read S's row, mask it by the reference's visible-key rule and
-//     keep the online softmax in base 2 (P = 2^(S·scale2 - m·scale2),
-//     l = l·α + ΣP).  The running maximum m is moved only when a row's scores
+//     TMEM lane).  Per chunk they read S's row, mask it by the reference's
+//     visible-key rule and keep the online softmax in base 2
+//     (P = 2^(S·scale2 - m·scale2), l = l·α + ΣP).  The running maximum m is moved only when a row's scores
 //     exceed it by more than 2^8, and only then is the row of O in TMEM
 //     rescaled by α (the result O / l does not depend on which m is used).
 //     P goes back into TMEM as bf16 (the precision the reference's own
@@ -129,7 +132,8 @@ __device__ __forceinline__ int tile_chunks(const AttnArgs& a, const RowDesc& rd,
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs a, PrefillPlan pl) {
+__global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                                    AttnArgs a, PrefillPlan pl) {
   using L = TcPrefillLayout<D>;
   const int G = a.nq / a.nkv;
   extern __shared__ uint8_t smem_raw[];
@@ -142,9 +146,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
   uint64_t* sfull = bars + 4;     // [tile] scores ready in TMEM
   uint64_t* pready = bars + 6;    // [tile] P written, O rescaled (the tile's four softmax warps)
   uint64_t* odone = bars + 8;     // [tile] value product done
-  uint64_t* qready = bars + 10;   // both tiles' query rows written (eight softmax warps)
-  uint64_t* drain = bars + 11;    // every MMA finished
-  uint32_t* tmem_holder = (uint32_t*)(bars + 12);
+  uint64_t* qfull = bars + 10;    // [tile] query rows landed
+  uint64_t* qempty = bars + 12;   // [tile] the item's score products read them
+  uint64_t* drain = bars + 14;    // every MMA finished
+  uint32_t* tmem_holder = (uint32_t*)(bars + 15);
   volatile int* abort_flag = (volatile int*)(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -156,7 +161,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       mbar_init(&pready[s], kSoftWarps / 2);
       mbar_init(&odone[s], 1);
     }
-    mbar_init(qready, kSoftWarps);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&qfull[x], 1);
+      mbar_init(&qempty[x], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -174,6 +182,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
   pdl_wait();  // the query rows and this forward's keys come from the kernel before
 
   long long issued = 0;
+  int qn[2] = {0, 0};  // query tile loads issued per tile (producer)
   if (warp == 0) {
     if (lane == 0) {
       long long n = 0;  // ring position of the next chunk
@@ -181,7 +190,22 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         int qa, b, h;
         pair_of(a, pl, i, qa, b, h);
         const RowDesc rd = a.rows[b];
-        const int nch = max(tile_chunks(a, rd, pl, b, qa), tile_chunks(a, rd, pl, b, qa + 1));
+        const int nx[2] = {tile_chunks(a, rd, pl, b, qa), tile_chunks(a, rd, pl, b, qa + 1)};
+        const int nch = max(nx[0], nx[1]);
+        // The tiles' query rows (tokens past the sequence read as zeros), once
+        // the previous item's score products of the tile have read theirs.
+        for (int x = 0; x < 2; ++x) {
+          if (nx[x] == 0) continue;
+          if (qn[x] > 0 && !mbar_wait(&qempty[x], (qn[x] - 1) & 1, a.err)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_expect_tx(&qfull[x], L::kQ);
+          for (int db = 0; db < L::kDB; ++db)
+            tma_load_4d(sq + x * L::kQ + db * kBoxT, &tm_q, &qfull[x], db * 64, h * G, (qa + x) * pl.tq, b);
+          ++qn[x];
+        }
+        if (*abort_flag) break;
         for (int ch = 0; ch < nch; ++ch, ++n) {
           const int s = (int)(n & 1);
           if (n >= 2 && !mbar_wait(&kvempty[s], (int)((n >> 1) - 1) & 1, a.err)) {
@@ -214,7 +238,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       long long n = 0;        // ring position of the item's first chunk
       long long kv_seen = 0;  // ring positions whose load this thread has waited for
       long long cnt[2] = {0, 0};  // chunks of each tile so far (its sfull / pready / odone phases)
-      int it = 0;
+      int qm[2] = {0, 0};         // query tiles of each tile so far (qfull / qempty phases)
       bool ok = true;
       auto wait_kv = [&](long long upto) -> bool {  // loads of ring positions < upto have landed
         for (; kv_seen < upto; ++kv_seen)
@@ -252,18 +276,22 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
         const RowDesc rd = a.rows[b];
         const int nx[2] = {tile_chunks(a, rd, pl, b, qa), tile_chunks(a, rd, pl, b, qa + 1)};
         const int nch = max(nx[0], nx[1]);
-        if (!mbar_wait(qready, it & 1, a.err)) {
-          ok = false;
-          break;
-        }
-        ++it;
         if (nch > 0) {
           if (!wait_kv(n + 1)) {
             ok = false;
             break;
           }
-          for (int x = 0; x < 2; ++x)
-            if (nx[x] > 0) score(x, n);
+          for (int x = 0; x < 2 && ok; ++x) {
+            if (nx[x] == 0) continue;
+            if (!mbar_wait(&qfull[x], qm[x] & 1, a.err)) {
+              ok = false;
+              break;
+            }
+            score(x, n);
+            if (nx[x] == 1) mma_commit(&qempty[x]);  // the tile's last score product
+            ++qm[x];
+          }
+          if (!ok) break;
         }
         for (int ch = 0; ch < nch && ok; ++ch) {
           for (int x = 0; x < 2 && ok; ++x) {
@@ -278,6 +306,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
                 break;
               }
               score(x, n + ch + 1);
+              if (ch + 2 == nx[x]) mma_commit(&qempty[x]);  // the tile's last score product
             }
           }
           mma_commit(&kvempty[(n + ch) & 1]);  // every product reading this chunk is issued
@@ -310,20 +339,6 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
       const bool valid = qt < pl.ntiles && r / G < pl.tq && s_tok < a.S;
       const int vis = valid ? visible(a, rd, b * a.S + s_tok, s_tok) : 0;
       const int tot = rd.past + a.S;  // keys written so far
-      // The query row into the tile (zeros for rows past the sequence).
-      {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            (const bf16*)a.q + (((size_t)b * a.S + (valid ? s_tok : 0)) * a.nq + (size_t)h * G + g) * D);
-        uint8_t* qd = sq + x * L::kQ;
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          const uint4 val = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(qd + swz_off(r, c)) = val;
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(qready);
 
       float m = -INFINITY, l = 0.f;  // m: the running maximum P is taken against (raw scores)
       for (int ch = 0; ch < nchx; ++ch, ++cnt) {
@@ -452,6 +467,8 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(AttnArgs 
     // Let the loads this CTA issued land before its shared memory goes away.
     for (long long i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
       mbar_wait(&kvfull[i & 1], (int)(i >> 1) & 1, a.err);
+    for (int x = 0; x < 2; ++x)
+      if (qn[x] > 0) mbar_wait(&qfull[x], (qn[x] - 1) & 1, a.err);
   }
   if (warp == 1 && lane == 0) mbar_wait(drain, 0, a.err);  // every MMA has finished
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -480,6 +497,23 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s) {
   pl.ntiles = (a.S + pl.tq - 1) / pl.tq;
   pl.items = (long long)((pl.ntiles + 1) / 2) * a.B * a.nkv;  // tile pairs
   if (pl.items <= 0) return cudaSuccess;
+  // The query rows as a 4-D bf16 array {D, nq, S, B}: a box of 64 dims x G
+  // heads x tq tokens x 1 row is one 64-wide block of a tile, rows in tile
+  // order (token r / G, head r % G); tokens past S read as zeros.
+  CUtensorMap tq;
+  {
+    tc_host::EncodeTiled enc = tc_host::encoder();
+    if (!enc) return cudaErrorNotSupported;
+    const cuuint64_t dims[4] = {(cuuint64_t)a.D, (cuuint64_t)a.nq, (cuuint64_t)a.S, (cuuint64_t)a.B};
+    const cuuint64_t strides[3] = {(cuuint64_t)a.D * 2, (cuuint64_t)a.nq * a.D * 2,
+                                   (cuuint64_t)a.S * a.nq * a.D * 2};
+    const cuuint32_t box[4] = {64, (cuuint32_t)G, (cuuint32_t)pl.tq, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (enc(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   auto go = [&](auto kernel, int smem) -> cudaError_t {
     static bool configured[2][64] = {};
     int dev = 0;
@@ -493,7 +527,7 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, cudaStream_t s) {
     }
     const long long cap = sm_count_prefill_tc();
     const int grid = (int)(pl.items < cap ? pl.items : cap);
-    return launch_pdl(kernel, dim3(grid), dim3(kThreadsT), smem, s, a, pl);
+    return launch_pdl(kernel, dim3(grid), dim3(kThreadsT), smem, s, tq, a, pl);
   };
   if (a.D == 128) return go(attn_prefill_tc_kernel<128>, TcPrefillLayout<128>::kBytes);
   return go(attn_prefill_tc_kernel<64>, TcPrefillLayout<64>::kBytes);
