@@ -412,7 +412,18 @@ def run_single(args) -> None:
     prefill_ms = t0.elapsed_time(t1)
     stage.check_device()  # a kernel that gave up waiting would make every number below meaningless
     ids = torch.cat(first).unsqueeze(-1)
-    prefill_attention = prefill_attention_rate(w, cfg, prompts[0].to(dev))
+
+    # The CPU baseline runs here, between the prefill and the decode region:
+    # under the prefill's GEMMs the power controller lowers the SM clock
+    # (1.44 GHz measured right after it), and it takes about 100 ms of decode
+    # to climb back to the 1.965 GHz a decode loop holds.  With the GPU idle
+    # while the host cores time the oracle, the decode region is measured at
+    # the clock decode runs at, not during that recovery.
+    base = None
+    if not args.no_cpu_baseline:
+        # bounded sample: 3 steps of the full batch (about 10 s of CPU work)
+        base = cpu_baseline(cfg, micro=args.micro, micro_batches=args.micro_batches, context=args.prompt,
+                            steps=3, warmup=1)
 
     rows_all = args.micro * args.micro_batches
 
@@ -472,6 +483,8 @@ def run_single(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = e2.elapsed_time(e3)
     stage.check_device()
+    # Prefill attention beside torch's SDPA (GEMM-heavy: after the decode region).
+    prefill_attention = prefill_attention_rate(w, cfg, prompts[0].to(dev))
 
     lin = prof["linear_decode"]
     att = prof["attention"]
@@ -488,12 +501,6 @@ def run_single(args) -> None:
     del workers, w, stage
     torch.cuda.empty_cache()
     longctx = None if args.no_long_context or args.model != "llama3-8b" else long_context(hbm)
-
-    base = None
-    if not args.no_cpu_baseline:
-        # bounded sample: 3 steps of the full batch (about 10 s of CPU work)
-        base = cpu_baseline(cfg, micro=args.micro, micro_batches=args.micro_batches, context=args.prompt,
-                            steps=3, warmup=1)
 
     traffic = NCU_TRAFFIC if args.model == "llama3-8b" else {
         k: {"dram_bytes": None, "algorithmic_bytes": None, "launches": None} for k in NCU_TRAFFIC}
