@@ -42,11 +42,18 @@ __device__ __forceinline__ void item_of(const AttnArgs& a, const PrefillPlan& pl
   h = rem % a.nkv;
 }
 
-// Keys the tile's last token sees: the item's chunk count follows from it.
+// The most keys any token of the tile sees: the item's chunk count follows
+// from it.  Without explicit positions a token sees min(past + s + 1, total)
+// keys (or all of them), which never decreases with s, so the tile's last
+// token decides; explicit positions can be in any order, so every token is
+// asked.  (Every role evaluates this at each work item's start, where the
+// per-token loop cost about 2000 cycles of the item boundary.)
 __device__ __forceinline__ int tile_keys(const AttnArgs& a, const RowDesc& rd, const PrefillPlan& pl, int b,
                                          int qt) {
   int s_hi = (qt + 1) * pl.tq;
   if (s_hi > a.S) s_hi = a.S;
+  if (s_hi <= qt * pl.tq) return 0;
+  if (a.positions == nullptr) return visible(a, rd, b * a.S + s_hi - 1, s_hi - 1);
   int kmax = 0;
   for (int s = qt * pl.tq; s < s_hi; ++s) kmax = max(kmax, visible(a, rd, b * a.S + s, s));
   return kmax;

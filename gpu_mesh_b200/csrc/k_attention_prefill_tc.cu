@@ -435,24 +435,28 @@ __global__ void __launch_bounds__(kThreadsT, 1) attn_prefill_tc_kernel(const __g
       }
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       bf16* out = (bf16*)a.out + (((size_t)b * a.S + (valid ? s_tok : 0)) * a.nq + (size_t)h * G + g) * D;
-#pragma unroll 1
-      for (int c4 = 0; c4 < D / 32; ++c4) {
-        float o[32];
+      {
+        // The row of O in one TMEM load (one wait), then 16-byte stores.
+        float o[D];
         if (nchx > 0) {
-          tmem_ld32(tmem + lanes + kColO + D * x + c4 * 32, o);
+          if constexpr (D == 128) {
+            tmem_ld128(tmem + lanes + kColO + D * x, o);
+          } else {
+            tmem_ld64(tmem + lanes + kColO + D * x, o);
+          }
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0.f;
+          for (int e = 0; e < D; ++e) o[e] = 0.f;
         }
         if (valid) {
 #pragma unroll
-          for (int e8 = 0; e8 < 4; ++e8) {
+          for (int e8 = 0; e8 < D / 8; ++e8) {
             uint4 w;
             w.x = pack2(o[8 * e8 + 0] * inv, o[8 * e8 + 1] * inv);
             w.y = pack2(o[8 * e8 + 2] * inv, o[8 * e8 + 3] * inv);
             w.z = pack2(o[8 * e8 + 4] * inv, o[8 * e8 + 5] * inv);
             w.w = pack2(o[8 * e8 + 6] * inv, o[8 * e8 + 7] * inv);
-            *reinterpret_cast<uint4*>(out + c4 * 32 + 8 * e8) = w;
+            *reinterpret_cast<uint4*>(out + 8 * e8) = w;
           }
         }
       }
