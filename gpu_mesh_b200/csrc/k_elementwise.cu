@@ -3,6 +3,8 @@
 // RMSNorm follows LlamaStage's RMSNorm.forward (models/llama_dense.py:91-93)
 // and HF Qwen3RMSNorm: mean of squares in fp32, multiply by 1/sqrt(ms + eps),
 // round to the activation dtype, then multiply by the weight in that dtype.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -184,6 +186,75 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_pieces_kernel(Pieces 
   }
 }
 
+// The same residual + RMSNorm with each row spread over a cluster of
+// kNormCluster CTAs of kNormThreads / kNormCluster threads, so a row's piece
+// loads come through four SMs instead of one (32 decode rows otherwise keep
+// 32 of 148 SMs busy).  CTA c's thread j plays thread 128·c + j of the
+// 512-thread kernel (same vectors, same order), each CTA writes its four
+// warp sums into all the cluster's CTAs, and after the cluster barrier every
+// CTA reduces the 16 warp sums exactly as block_sum does: the outputs are
+// bit-identical to resid_norm_pieces_kernel's.  Every CTA of a cluster takes
+// the same branches (the only early return depends on a kernel argument), so
+// all of them reach the barrier.
+constexpr int kNormCluster = 4;
+constexpr int kNormCtaThreads = kNormThreads / kNormCluster;
+
+__global__ void __launch_bounds__(kNormCtaThreads) resid_norm_pieces_cluster_kernel(
+    Pieces pc, __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, int H, float eps,
+    __nv_bfloat16* __restrict__ y) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  pdl_trigger();
+  const int c = (int)cluster.block_rank();
+  const int t = c * kNormCtaThreads + (int)threadIdx.x;  // thread of the 512-thread kernel
+  const bool one = w && H / 8 <= kNormThreads;
+  float g0[8];
+  if (one && t < H / 8) load16_f<__nv_bfloat16>(w + t * 8, g0);
+  pdl_wait();
+  __shared__ float red[32];
+  const int m = blockIdx.x / kNormCluster;
+  __nv_bfloat16* xr = x + (size_t)m * H;
+  float ss = 0.f;
+  for (int i = t; i < H / 8; i += kNormThreads) {
+    float acc[8], v[8];
+    pieces_sum8(pc, m, i * 8, acc);
+    load16_f<__nv_bfloat16>(xr + i * 8, v);
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o[j] = __float2bfloat16_rn(v[j] + rt<__nv_bfloat16>(acc[j]));
+      const float nv = __bfloat162float(o[j]);
+      ss += nv * nv;
+    }
+    *reinterpret_cast<uint4*>(xr + i * 8) = *reinterpret_cast<const uint4*>(o);
+  }
+  if (!w) return;
+  // block_sum over the cluster: warp sums first, each written into every CTA.
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int r = 0; r < kNormCluster; ++r) cluster.map_shared_rank(red, r)[c * (kNormCtaThreads / 32) + warp] = ss;
+  cluster.sync();
+  constexpr int nw = kNormThreads / 32;
+  float tsum = lane < nw ? red[lane] : 0.f;
+  tsum = warp_sum(tsum);
+  const float r = 1.0f / sqrtf(tsum / (float)H + eps);
+  __nv_bfloat16* yr = y + (size_t)m * H;
+  for (int i = t; i < H / 8; i += kNormThreads) {
+    float v[8], g[8], o[8];
+    load16_f<__nv_bfloat16>(xr + i * 8, v);  // this thread's own stores
+    if (one) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) g[j] = g0[j];
+    } else {
+      load16_f<__nv_bfloat16>(w + i * 8, g);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = rt<__nv_bfloat16>(rt<__nv_bfloat16>(v[j] * r) * g[j]);
+    store16_f<__nv_bfloat16>(yr + i * 8, o);
+  }
+}
+
 template <typename T>
 __global__ void kv_copy_kernel(T* __restrict__ kv, int layer, int kvsel, int slot_rows, int nkv,
                                int cap, int D, int len, T* __restrict__ ext, bool to_slot) {
@@ -221,8 +292,32 @@ cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const
                                      int H, float eps, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (dtype != kBF16 || H % 8 || !pc.slots) return cudaErrorInvalidValue;
-  { const cudaError_t _le = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(kNormThreads), 0, s, pc, (__nv_bfloat16*)x,
-                                        (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn); if (_le != cudaSuccess) return _le; }
+  // A cluster of four CTAs per row (bit-identical to the one-CTA kernel,
+  // which MESHGPU_NORM_ONE_CTA=1 selects; its tests compare the two).
+  const char* one_cta = getenv("MESHGPU_NORM_ONE_CTA");
+  if (one_cta && one_cta[0] == '1') {
+    const cudaError_t e = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(kNormThreads), 0, s, pc,
+                                     (__nv_bfloat16*)x, (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M * kNormCluster);
+  cfg.blockDim = dim3(kNormCtaThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kNormCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, resid_norm_pieces_cluster_kernel, pc, (__nv_bfloat16*)x,
+                                           (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn);
+  note_launch();
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

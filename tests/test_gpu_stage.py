@@ -346,3 +346,36 @@ def test_rope_kv_append_matches_oracle(dtype, D, nq, nkv, qk_norm, S):
 
 def tol_logits(dtype, ref: torch.Tensor) -> float:
     return 1e-4 * float(ref.abs().max()) if dtype == torch.float32 else 2e-2
+
+
+def test_decode_norm_cluster_kernel_is_bit_identical_to_one_cta(monkeypatch):
+    """The decode residual + RMSNorm spreads each row over a cluster of four
+    CTAs; it keeps the one-CTA kernel's reduction order, so two stages with
+    the same weights, one per kernel (MESHGPU_NORM_ONE_CTA=1 selects the
+    one-CTA kernel), give identical logits at the Llama-3-8B width."""
+    cfg = LlamaConfig(vocab_size=2048, hidden_size=4096, intermediate_size=14336, num_hidden_layers=2,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=512,
+                      rope_theta=500000.0)
+    full = synthetic_model_state(cfg, seed=7, dtype=torch.bfloat16, device=DEV, method="portable")
+    a = build_pipeline(cfg, 1, [DEV], transport="local_cuda", dtype=torch.bfloat16, state_dict=full)[0]
+    b = build_pipeline(cfg, 1, [DEV], transport="local_cuda", dtype=torch.bfloat16, state_dict=full)[0]
+    del full
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (8, 40), generator=g).to(DEV)
+    with torch.no_grad():
+        a.forward_inference(None, input_ids=ids, operation_id=1, attempt_id="a", cache_key="k")
+        b.forward_inference(None, input_ids=ids, operation_id=1, attempt_id="a", cache_key="k")
+        tok = torch.randint(0, cfg.vocab_size, (8, 1), generator=g).to(DEV)
+        for step in range(3):
+            la = a.forward_inference(None, input_ids=tok, operation_id=2 + step, attempt_id="a",
+                                     cache_key="k").output.float().cpu()
+            monkeypatch.setenv("MESHGPU_NORM_ONE_CTA", "1")
+            lb = b.forward_inference(None, input_ids=tok, operation_id=2 + step, attempt_id="a",
+                                     cache_key="k").output.float().cpu()
+            monkeypatch.delenv("MESHGPU_NORM_ONE_CTA")
+            assert torch.equal(la, lb), step
+            tok = la[:, -1].argmax(-1, keepdim=True).to(DEV)
+    a.check_device()
+    b.check_device()
+    a.close()
+    b.close()
