@@ -250,6 +250,18 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
   } else {
     // Consumers: warp w owns keys 16w .. 16w + 15 of each chunk and keeps an
     // online softmax (max, sum, O) over the chunks of the current pair.
+    // The first piece's visible length (from its row descriptor) does not depend on
+    // the kernel before this one (the row table is uploaded before the
+    // forward's first kernel, as the producer's early loads assume; without
+    // explicit positions the visible length follows from it), so they are
+    // read before the programmatic-launch wait instead of after it (about a
+    // microsecond of each launch's start).
+    const bool early = a.positions == nullptr && u0 < u1;
+    int nvis0 = 0;
+    if (early) {
+      const int m0 = (int)(u0 / C / a.nkv);
+      nvis0 = visible(a, a.rows[m0 / a.S], m0, m0 % a.S);
+    }
     pdl_wait();
     const int g = lane >> 2, t = lane & 3;
     // Scores are kept in base 2 (scale·log2 e folded in), so every
@@ -260,8 +272,7 @@ __global__ void __launch_bounds__(kThreadsA, 1) attn_tc_kernel(AttnArgs a, Plan 
       const long long p = u / C;
       const long long pe = min(u1, (p + 1) * (long long)C);
       const int m = (int)(p / a.nkv), h = (int)(p % a.nkv);
-      const RowDesc rd = a.rows[m / a.S];
-      const int nvis = visible(a, rd, m, m % a.S);
+      const int nvis = early && u == u0 ? nvis0 : visible(a, a.rows[m / a.S], m, m % a.S);
       const int kb = (int)(u - p * C), ke = (int)(pe - p * C);
       const int kl = min(ke, (nvis + kChunk - 1) / kChunk);  // chunks [kb, kl) hold visible keys
 
