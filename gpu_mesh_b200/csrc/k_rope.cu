@@ -112,7 +112,6 @@ inline int sm_count_cached() {
 template <typename T, int D>
 __global__ void __launch_bounds__(kVecWarps * 32) qkv_post_pieces_kernel(QkvPostArgs a) {
   pdl_trigger();
-  pdl_wait();
   constexpr int VEC = 16 / sizeof(T), LPH = D / VEC, HPW = 32 / LPH, half = D / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPH, hl = lane % LPH;
@@ -121,12 +120,31 @@ __global__ void __launch_bounds__(kVecWarps * 32) qkv_post_pieces_kernel(QkvPost
   const int nh = a.nq + 2 * a.nkv;
   const int groups = (nh + HPW - 1) / HPW;
   const long long units = (long long)a.B * a.S * groups;
-  for (long long u = (long long)blockIdx.x * kVecWarps + warp; u < units; u += (long long)gridDim.x * kVecWarps) {
+  const long long u_first = (long long)blockIdx.x * kVecWarps + warp;
+  // The first unit's row descriptor and rotary table entries do not depend on
+  // the kernel before this one (the row table is uploaded before the
+  // forward's first kernel, the tables at stage creation; without explicit
+  // positions the position follows from the row), so they are read before
+  // the programmatic-launch wait, leaving only the piece loads after it.
+  const bool early = a.positions == nullptr && u_first < units;
+  RowDesc rd0{};
+  float c0[VEC], s0[VEC];
+  if (early) {
+    const int m = (int)(u_first / groups);
+    rd0 = a.rows[m / a.S];
+    int64_t pos = (int64_t)rd0.past + m % a.S;
+    pos = pos < 0 ? 0 : (pos >= a.max_pos ? a.max_pos - 1 : pos);
+    load16_f<T>((const T*)a.cos + (size_t)pos * half + dh, c0);
+    load16_f<T>((const T*)a.sin + (size_t)pos * half + dh, s0);
+  }
+  pdl_wait();
+  for (long long u = u_first; u < units; u += (long long)gridDim.x * kVecWarps) {
+    const bool first = early && u == u_first;
     const int m = (int)(u / groups);
     const int hh = (int)(u % groups) * HPW + sub;
     const bool valid = hh < nh;  // lanes past the last head still join the shuffles
     const int b = m / a.S, s = m % a.S;
-    const RowDesc rd = a.rows[b];
+    const RowDesc rd = first ? rd0 : a.rows[b];
     const int cache_pos = rd.past + s;
     int64_t pos = a.positions ? a.positions[m] : (int64_t)cache_pos;
     if (pos < 0 || pos >= a.max_pos) {
@@ -168,8 +186,13 @@ __global__ void __launch_bounds__(kVecWarps * 32) qkv_post_pieces_kernel(QkvPost
       }
     }
     float c[VEC], sv[VEC], y[VEC];
-    load16_f<T>((const T*)a.cos + (size_t)pos * half + dh, c);
-    load16_f<T>((const T*)a.sin + (size_t)pos * half + dh, sv);
+    if (first) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) c[i] = c0[i], sv[i] = s0[i];
+    } else {
+      load16_f<T>((const T*)a.cos + (size_t)pos * half + dh, c);
+      load16_f<T>((const T*)a.sin + (size_t)pos * half + dh, sv);
+    }
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const float partner = __shfl_xor_sync(0xffffffffu, x[i], LPH / 2);
