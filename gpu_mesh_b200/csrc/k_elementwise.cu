@@ -314,10 +314,18 @@ cudaError_t launch_resid_norm_pieces(int dtype, const Pieces& pc, void* x, const
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, resid_norm_pieces_cluster_kernel, pc, (__nv_bfloat16*)x,
-                                           (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, resid_norm_pieces_cluster_kernel, pc, (__nv_bfloat16*)x,
+                                     (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn);
+  if (e != cudaSuccess) {
+    // A device or partition that cannot place a cluster of four: the
+    // one-CTA kernel (same rows, bit for bit).
+    cudaGetLastError();
+    e = launch_pdl(resid_norm_pieces_kernel, dim3(M), dim3(kNormThreads), 0, s, pc, (__nv_bfloat16*)x,
+                   (const __nv_bfloat16*)w, H, eps, (__nv_bfloat16*)xn);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
   note_launch();
-  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
